@@ -1,0 +1,396 @@
+"""Benchmark of the B200 GGUF quantized-matmul path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload (the metric's "Q4_K GEMV"): decode
+of one Llama-3-8B-shaped layer, M=1 token, every projection Q4_K:
+q 4096->4096, k/v 4096->1024, o 4096->4096, gate/up 4096->14336,
+down 14336->4096 (218,103,808 weights = 122,683,392 bytes of GGUF blocks).
+One step = the 7 GEMV launches of one layer. ``value`` is the whole-job
+algorithmic HBM throughput (weight bytes + activation bytes read + output
+bytes written, per step) in GB/s, timed with CUDA events on the launching
+stream, weights resident in HBM. The weights rotate over 3 copies
+(368 MB > 126 MB L2) so no step is served from L2.
+
+Also reported: ``e2e`` (same metric through the public Python API with the
+activations copied from pinned host memory and the outputs read back every
+step), ``roofline`` for the dominant kernel, ``prefill`` (config 4 tensor-core
+GEMM TFLOP/s), ``cpu_baseline`` (the reference's CPU arithmetic: gguf-py
+dequantize + numpy fp32 matmul on a bounded sample) and sampled clocks.
+
+Multi-GPU (torchrun, one process per GPU): every rank decodes its own layer
+(independent weights, no collective in the data path) -> weak scaling;
+value = all ranks' bytes / max-over-ranks time.
+
+``--impl reference`` times the reference's own CPU path for the same metric:
+gguf.quants.dequantize (gguf-py, the reference's pinned dependency) followed
+by a numpy fp32 matmul, on rank 0 only, over a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vllm-webgpu_b200"))
+
+LAYER = [  # (name, N = out features, K = in features) -- Llama-3-8B layer
+    ("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096), ("o_proj", 4096, 4096),
+    ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096), ("down_proj", 4096, 14336),
+]
+Q4_K = 12
+QK_BYTES = 144 / 256  # bytes per Q4_K weight
+METRIC = "Q4_K GEMV HBM GB/s (% of peak); prefill dequant-GEMM TFLOP/s at 1/2/4/8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def layer_bytes(m: int = 1, act_bytes: int = 2, out_bytes: int = 4) -> int:
+    """Algorithmic bytes of one layer decode: GGUF weight blocks + x read + y written."""
+    total = 0
+    for _, n, k in LAYER:
+        total += n * k // 256 * 144 + m * k * act_bytes + m * n * out_bytes
+    return total
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = [r.split(",") for r in (self.out or "").strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def read_traffic(kernel_tag: str):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", f"{kernel_tag}.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch_full_layer_step:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference's quantized matmul arithmetic on host cores
+# ----------------------------------------------------------------------------
+
+def cpu_reference_rate(budget_s: float, seed: int = 0) -> dict:
+    """gguf.quants.dequantize + numpy fp32 matmul over row slabs of the layer's
+    projections, for about ``budget_s`` seconds. Returns GB/s of the same
+    algorithmic bytes (GGUF blocks + activations + outputs)."""
+    import numpy as np
+    try:
+        from gguf import GGMLQuantizationType
+        from gguf.quants import dequantize as deq
+        kind, how = "reference", "gguf-py 0.19 quants.dequantize + numpy fp32 matmul"
+        qtype = GGMLQuantizationType.Q4_K
+    except ImportError:  # the oracle port restates the same arithmetic
+        from oracle import gguf_oracle as O
+        kind, how = "port", "oracle numpy restatement of gguf dequantize + numpy fp32 matmul"
+        qtype = O.Q4_K
+
+        def deq(raw, qt):
+            return O.dequantize(raw, qt)
+    rng = np.random.default_rng(seed)
+    slab_rows = 512
+    # per projection: a slab of random (but valid-format) Q4_K rows, x ~ N(0,1)
+    work = []
+    for name, n, k in LAYER:
+        raw = rng.integers(0, 256, size=(slab_rows, k // 256 * 144), dtype=np.uint8)
+        hdr = raw.reshape(slab_rows, -1, 144)
+        hdr[:, :, 0:2] = np.array([1e-3], np.float16).view(np.uint8)  # finite d / dmin
+        hdr[:, :, 2:4] = np.array([1e-3], np.float16).view(np.uint8)
+        x = rng.standard_normal((1, k)).astype(np.float32)
+        work.append((raw, x, slab_rows, k))
+    done_bytes = 0
+    t0 = time.perf_counter()
+    t_deq = t_mm = 0.0
+    while True:
+        for raw, x, n, k in work:
+            a = time.perf_counter()
+            w = deq(raw, qtype).reshape(n, k)
+            b = time.perf_counter()
+            _ = x @ w.T
+            c = time.perf_counter()
+            t_deq += b - a
+            t_mm += c - b
+            done_bytes += raw.nbytes + k * 2 + n * 4
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    threads = os.environ.get("OMP_NUM_THREADS") or str(os.cpu_count())
+    return {"value": done_bytes / dt / 1e9, "unit": "GB/s", "cores": int(threads), "kind": kind,
+            "sample": (f"{how}; {slab_rows}-row slabs of each of the 7 Llama-3-8B Q4_K projections, M=1, "
+                       f"{dt:.1f} s ({t_deq:.1f} s dequant, {t_mm:.1f} s matmul); BLAS threads={threads}, "
+                       f"os.cpu_count()={os.cpu_count()}")}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    total_steps = args.steps + args.warmup
+    # bounded: the whole run ends within about 90 s whatever K is
+    per_step = max(0.002, min(5.0, 90.0 / max(1, total_steps)))
+    budget = per_step * args.steps
+    res = cpu_reference_rate(budget)
+    line = {
+        "metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4/u6 x fp32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
+                   "parallelism": "rank 0 only (CPU)"},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int) -> None:
+    import torch
+    import torch.distributed as dist
+    from vllm_webgpu_b200 import ops
+    from vllm_webgpu_b200.quant.pack import random_weights
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    peaks, peak_src = load_peaks()
+    m = 1
+    copies = 3
+    # weights: 3 independent copies of the layer (seeded per rank and copy)
+    layers = []
+    for c in range(copies):
+        layers.append([random_weights(n, k, Q4_K, seed=1000 * rank + 10 * c + i, device=dev)
+                       for i, (_, n, k) in enumerate(LAYER)])
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    xs = {k: torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16) for k in (4096, 14336)}
+    ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _, n, _ in LAYER]
+    stream = torch.cuda.current_stream(dev)
+
+    def step(c: int) -> None:
+        for i, (_, n, k) in enumerate(LAYER):
+            ops.gemv(xs[k], layers[c][i], out=ys[i])
+
+    # warm-up (also primes attributes / driver entry points before capture)
+    for i in range(max(3, args.warmup)):
+        step(i % copies)
+    torch.cuda.synchronize()
+
+    # one CUDA graph holding a step on each weight copy (launch overhead out of the device time)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for c in range(copies):
+            step(c)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    reps = max(1, args.steps // copies)
+    steps = reps * copies
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    step_bytes = layer_bytes(m, act_bytes=2, out_bytes=4)
+    value = step_bytes * steps * world / (ms / 1e3) / 1e9
+
+    # per-launch timing of the dominant kernel (every launch is gemv_kernel<Q4_K,1,1>)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(LAYER))]
+    per = [0.0] * len(LAYER)
+    nrep = 30
+    for r in range(nrep):
+        c = r % copies
+        for i, (_, n, k) in enumerate(LAYER):
+            ev[2 * i].record(stream)
+            ops.gemv(xs[k], layers[c][i], out=ys[i])
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        for i in range(len(LAYER)):
+            per[i] += ev[2 * i].elapsed_time(ev[2 * i + 1]) / nrep
+    kern_ms = sum(per)
+    achieved = step_bytes / (kern_ms / 1e3) / 1e9
+    # end to end through the public API: pinned host x -> device, 7 projections, y -> pinned host
+    hx = {k: torch.randn((m, k)).to(torch.bfloat16).pin_memory() for k in (4096, 14336)}
+    hy = [torch.empty((m, n), dtype=torch.float32).pin_memory() for _, n, _ in LAYER]
+    e2e_steps = max(30, min(2000, steps // 10))
+    h2d = sum(m * k * 2 for _, _, k in LAYER)
+    d2h = sum(m * n * 4 for _, n, _ in LAYER)
+
+    def e2e_step(c: int) -> None:
+        for i, (_, n, k) in enumerate(LAYER):
+            xd = hx[k].to(dev, non_blocking=True)
+            yd = ops.mul_mat(xd, layers[c][i], out_dtype=torch.float32)
+            hy[i].copy_(yd, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(5):
+        e2e_step(i % copies)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i % copies)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9
+
+    # prefill (config 4): Q4_K GEMM M=2048, K=4096, N=14336 on the tensor cores
+    pre = None
+    if not args.no_prefill:
+        pm, pn, pk = 2048, 14336, 4096
+        wq = layers[0][4]  # gate_proj: 14336 x 4096
+        xp = torch.randn((pm, pk), device=dev).to(torch.bfloat16)
+        yp = torch.empty((pm, pn), dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            ops.gemm(xp, wq, out=yp)
+        torch.cuda.synchronize()
+        it = 10
+        e0.record(stream)
+        for _ in range(it):
+            ops.gemm(xp, wq, out=yp)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        pms = e0.elapsed_time(e1) / it
+        tf = 2.0 * pm * pn * pk / (pms / 1e3) / 1e12
+        pre = {"workload": "q4k_prefill_m2048_k4096_n14336", "ms": round(pms, 4), "tflops": round(tf, 2),
+               "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
+               "path": "dequant->fp16 workspace + tcgen05 GEMM (2 kernels)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_rate(args.cpu_seconds)
+
+    if rank == 0:
+        clocks = clk.summary()
+        peak = float(peaks["hbm_gbs"])
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / steps, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u4 x bf16 -> fp32", "data": "synthetic",
+            "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
+                       "projections": {nm: [k, n] for nm, n, k in LAYER},
+                       "weight_bytes_per_step": sum(n * k // 256 * 144 for _, n, k in LAYER),
+                       "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
+                       "graph": "CUDA graph of 3 steps", "parallelism": f"dp{world} (independent layer per rank)"},
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K,M=1>", "achieved": round(achieved, 2),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": read_traffic("gemv_q4k_layer_m1"), "peak_source": peak_src,
+                         "per_launch_us": {nm: round(per[i] * 1e3, 2) for i, (nm, _, _) in enumerate(LAYER)}},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "path": "ops.mul_mat per projection, pinned host buffers"},
+            "gpu_launches": len(LAYER) * steps,
+            "clocks": clocks,
+            "prefill": pre,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=30)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl")
+    try:
+        run_ours(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,152 @@
+/*
+ * ggufmm.h -- C ABI of the B200 (sm_100a) GGUF block-quantized matmul library
+ * (libggufmm.so).
+ *
+ * The library replaces the quantized-matmul dispatch of maci0/vllm-webgpu:
+ * the WGSL kernels vllm_webgpu/shaders/generic/matmul_quant.wgsl:20-61
+ * (decode GEMV) and matmul_quant_mr4.wgsl:77-131 (multi-row "prefill"), which
+ * the models reach through BaseWebGPUModel._dispatch("matmul_quant",
+ * [x, W, scales, out], {K, N, USE_QUANT}, ...) (vllm_webgpu/models/base.py:62-100,
+ * call sites vllm_webgpu/models/llama.py:276-283,328-332,343-348,355-359).
+ * Weights are GGUF blocks exactly as gguf.GGUFReader yields them
+ * (vllm_webgpu/quant/gguf_loader.py:137-162): row-major [N, K/block*type_size]
+ * bytes, never repacked.
+ *
+ * Conventions (all entry points):
+ *   - every pointer is a caller-owned DEVICE pointer; nothing here allocates
+ *     device memory (the GEMM takes an explicit workspace);
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream); work is stream-ordered and no entry point synchronizes;
+ *   - the return value is GGUFMM_OK (0) or a negative GGUFMM_ERR_* code.
+ *     Argument errors are detected on the host before any launch, so a
+ *     failed call enqueues nothing. The reference raised ValueError for bad
+ *     shapes (vllm_webgpu/models/llama.py:45-54); the Python binding maps the
+ *     codes back to ValueError / RuntimeError;
+ *   - entry points are thread-safe and may be called concurrently on
+ *     different streams.
+ */
+#ifndef GGUFMM_H_
+#define GGUFMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GGUFMM_VERSION 100 /* 1.0.0 */
+
+/* Quantization types: the GGMLQuantizationType ids of gguf-py
+ * (gguf/constants.py:4059-4073), which GGUFReader reports per tensor. */
+enum ggufmm_qtype {
+  GGUFMM_Q4_0 = 2,  /* 32 weights / 18 B: fp16 d, 16 B nibbles            */
+  GGUFMM_Q8_0 = 8,  /* 32 weights / 34 B: fp16 d, 32 x int8               */
+  GGUFMM_Q4_K = 12, /* 256 weights / 144 B: fp16 d,dmin, 12 B 6-bit sc/m, 128 B nibbles */
+  GGUFMM_Q6_K = 14  /* 256 weights / 210 B: 128 B ql, 64 B qh, 16 x int8 sc, fp16 d */
+};
+
+/* Element types of activations and outputs. */
+enum ggufmm_dtype {
+  GGUFMM_F32 = 0,
+  GGUFMM_F16 = 1,
+  GGUFMM_BF16 = 2
+};
+
+enum ggufmm_status {
+  GGUFMM_OK = 0,
+  GGUFMM_ERR_QTYPE = -1,     /* unsupported quantization type            */
+  GGUFMM_ERR_SHAPE = -2,     /* K not a multiple of the block, M/N/K <= 0 or too large */
+  GGUFMM_ERR_ALIGN = -3,     /* a pointer is not aligned as required      */
+  GGUFMM_ERR_DTYPE = -4,     /* unsupported activation / output dtype     */
+  GGUFMM_ERR_WORKSPACE = -5, /* workspace NULL or smaller than required   */
+  GGUFMM_ERR_CUDA = -6,      /* a CUDA launch or device query failed      */
+  GGUFMM_ERR_ARG = -7,       /* NULL pointer or other invalid argument    */
+  GGUFMM_ERR_DEVICE = -8     /* the current device is not sm_100          */
+};
+
+/* Library version (GGUFMM_VERSION of the build). */
+int ggufmm_version(void);
+
+/* Block geometry of a qtype: weights per block / bytes per block; 0 when the
+ * qtype is unsupported. Mirrors gguf GGML_QUANT_SIZES (constants.py:4231-4245). */
+int ggufmm_block_size(int qtype);
+int ggufmm_type_size(int qtype);
+
+/* Human-readable text for a status code (static storage). */
+const char* ggufmm_status_string(int status);
+
+/* The last CUDA error code seen by this thread inside the library (0 if none). */
+int ggufmm_last_cuda_error(void);
+
+/*
+ * Device-side status word: every spin-wait inside the kernels is bounded and,
+ * when it gives up, ORs 1 into this word and unwinds instead of hanging.
+ * Returns the word (>= 0; 0 = no timeout seen) or a negative status.
+ * Synchronizes `stream`; clears the word when `clear` is nonzero.
+ */
+int ggufmm_device_status(int clear, void* stream);
+
+/*
+ * Dequantize `n_rows` rows of `k` weights: out[n, k] (row-major, out_dtype
+ * F32 or F16). With out_dtype F32 the result is bit-identical to
+ * gguf.quants.dequantize (gguf quants.py:241-251, 396-401, 504-522, 555-572),
+ * which is what the reference's loader decodes with
+ * (vllm_webgpu/quant/gguf_loader.py:143-159). F16 rounds that fp32 value once
+ * (round-to-nearest-even). `q` needs 2-byte alignment, `out` 16-byte.
+ */
+int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k,
+                      void* out, int out_dtype, void* stream);
+
+/*
+ * Decode GEMV: y[m, n] = sum_k x[m, k] * W[n, k] for 1 <= M <= 8 tokens.
+ * Replaces matmul_quant.wgsl:20-61 (one thread per output row there).
+ *   q       GGUF blocks [N, K/block*type_size], 16-byte aligned base
+ *   x       activations [M, K], row stride `ldx` elements (>= K), x_dtype
+ *           F32 / F16 / BF16
+ *   y       outputs [M, N], row stride `ldy` elements (>= N), y_dtype
+ *           F32 / F16 / BF16
+ * fp32 accumulation; max|y - y_ref| / rms(y_ref) <= 2e-3 against the fp32
+ * dequantize-then-matmul.
+ */
+int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k,
+                const void* x, int x_dtype, int64_t m, int64_t ldx,
+                void* y, int y_dtype, int64_t ldy, void* stream);
+
+/*
+ * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
+ * arguments). Size it once for the largest M and reuse it.
+ */
+size_t ggufmm_gemm_workspace_size(int qtype, int64_t m, int64_t n, int64_t k);
+
+/*
+ * Prefill / batched GEMM on the sm_100a tensor cores (tcgen05.mma with TMEM
+ * accumulators, operands staged by TMA): y[m, n] = sum_k x[m, k] * W[n, k],
+ * any M >= 1. Replaces the never-dispatched matmul_quant_mr4.wgsl:77-131
+ * (and the token-at-a-time prefill of run_inference.py:323-350). Operands are
+ * fp16 (the dequantized fp32 weight rounded once; bf16 activations convert
+ * exactly), accumulation fp32. Same layout and error gate as ggufmm_gemv.
+ * `workspace` (device, 256-byte aligned) must hold
+ * ggufmm_gemm_workspace_size() bytes; its contents are scratch.
+ */
+int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k,
+                const void* x, int x_dtype, int64_t m, int64_t ldx,
+                void* y, int y_dtype, int64_t ldy,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * y = x @ W^T choosing the kernel by M (GEMV for M <= 8, GEMM otherwise), the
+ * way vLLM's GGUF linear method picks between its GEMV and GEMM kernels
+ * (vllm/model_executor/layers/quantization/gguf.py:198-230). The workspace
+ * may be NULL when M <= 8.
+ */
+int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k,
+                   const void* x, int x_dtype, int64_t m, int64_t ldx,
+                   void* y, int y_dtype, int64_t ldy,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGUFMM_H_ */

@@ -1,0 +1,82 @@
+"""The C ABI: the library loads, exports every declared symbol and rejects bad
+arguments on the host before touching a GPU (CPU only)."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+from tests.helpers import header_functions
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from vllm_webgpu_b200 import _lib
+    return _lib.load()
+
+
+def test_header_declares_the_entry_points():
+    names = header_functions()
+    for must in ("ggufmm_dequantize", "ggufmm_gemv", "ggufmm_gemm", "ggufmm_mul_mat",
+                 "ggufmm_gemm_workspace_size", "ggufmm_version"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from vllm_webgpu_b200 import _lib
+    for name in header_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_geometry(lib):
+    assert lib.ggufmm_version() >= 100
+    assert [lib.ggufmm_block_size(q) for q in (2, 8, 12, 14)] == [32, 32, 256, 256]
+    assert [lib.ggufmm_type_size(q) for q in (2, 8, 12, 14)] == [18, 34, 144, 210]
+    assert lib.ggufmm_block_size(3) == 0 and lib.ggufmm_type_size(99) == 0
+
+
+def test_workspace_size(lib):
+    assert lib.ggufmm_gemm_workspace_size(12, 512, 14336, 4096) == 14336 * 4096 * 2 + 512 * 4096 * 2
+    assert lib.ggufmm_gemm_workspace_size(12, 1, 10, 100) == 0  # K not a block multiple
+    assert lib.ggufmm_gemm_workspace_size(99, 1, 10, 256) == 0
+
+
+def _gemv(lib, q=1 << 20, qt=12, n=16, k=256, x=1 << 20, xt=2, m=1, ldx=256, y=1 << 20, yt=0, ldy=16):
+    return lib.ggufmm_gemv(q, qt, n, k, x, xt, m, ldx, y, yt, ldy, None)
+
+
+def test_host_side_validation(lib):
+    from vllm_webgpu_b200 import _lib as L
+    assert _gemv(lib, q=None) == L.ERR_ARG
+    assert _gemv(lib, qt=3) == L.ERR_QTYPE
+    assert _gemv(lib, k=100) == L.ERR_SHAPE
+    assert _gemv(lib, m=9) == L.ERR_SHAPE
+    assert _gemv(lib, m=0) == L.ERR_SHAPE
+    assert _gemv(lib, ldx=128) == L.ERR_SHAPE
+    assert _gemv(lib, xt=7) == L.ERR_DTYPE
+    assert _gemv(lib, q=(1 << 20) + 8) == L.ERR_ALIGN
+    assert lib.ggufmm_dequantize(None, 12, 1, 256, 1 << 20, 0, None) == L.ERR_ARG
+    assert lib.ggufmm_dequantize(1 << 20, 12, 1, 256, 1 << 20, 2, None) == L.ERR_DTYPE
+    assert lib.ggufmm_gemm(1 << 20, 12, 16, 256, 1 << 20, 2, 32, 256, 1 << 20, 0, 16, None, 0, None) == L.ERR_WORKSPACE
+    assert b"block size" in lib.ggufmm_status_string(L.ERR_SHAPE)
+
+
+def test_status_maps_to_reference_exceptions():
+    from vllm_webgpu_b200 import _lib as L
+    with pytest.raises(ValueError):
+        L.check(L.ERR_SHAPE, "x")
+    with pytest.raises(L.GGUFMMError):
+        L.check(L.ERR_CUDA, "x")
+    L.check(L.OK, "x")
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from vllm_webgpu_b200 import ops
+    from vllm_webgpu_b200.formats import GGUFQuantTensor
+    w = GGUFQuantTensor(torch.zeros((4, 144), dtype=torch.uint8), 12, (4, 256))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gemv(torch.zeros((1, 256)), w)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.dequantize(w)

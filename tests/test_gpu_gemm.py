@@ -1,0 +1,92 @@
+"""Tensor-core (tcgen05) GEMM against the fp32 dequantize-then-matmul oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gguf_oracle as O
+from tests.helpers import QTYPES, QNAMES, TOL, golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _wt(raw, qt, n, k):
+    from vllm_webgpu_b200.formats import GGUFQuantTensor
+    return GGUFQuantTensor(torch.from_numpy(np.ascontiguousarray(raw).reshape(n, -1)).cuda(), qt, (n, k))
+
+
+def _check(qt, m, n, k, seed=0, rows=None, ydtype=torch.float32):
+    from vllm_webgpu_b200 import ops
+    raw = O.make_weights(n, k, qt, seed=seed)
+    x = torch.from_numpy(O.make_activations(m, k, seed=seed + 1)).to(torch.bfloat16).cuda()
+    y = ops.gemm(x, _wt(raw, qt, n, k), out_dtype=ydtype)
+    torch.cuda.synchronize()
+    y = y.float().cpu().numpy()
+    xf = x.float().cpu().numpy()
+    if rows is not None:  # check a sample of output columns (weight rows)
+        idx = np.random.default_rng(seed).choice(n, size=rows, replace=False)
+        idx.sort()
+        ref = O.matmul_ref(xf, raw[idx], qt, rows, k)
+        return O.rel_err(y[:, idx], ref)
+    return O.rel_err(y, O.matmul_ref(xf, raw, qt, n, k))
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("m", [9, 16, 33, 64, 100, 256, 300])
+def test_gemm_small(cuda, qt, m):
+    assert _check(qt, m, 1024, 4096) <= TOL
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("n,k", [(200, 512), (130, 2048), (4096, 14336)])
+def test_gemm_ragged(cuda, qt, n, k):
+    assert _check(qt, 77, n, k) <= TOL
+
+
+@pytest.mark.parametrize("qt", [O.Q4_K, O.Q6_K], ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("m", [512, 2048])
+def test_gemm_prefill_config(cuda, qt, m):
+    """BASELINE config 4 (K=4096, N=14336), 384 sampled weight rows checked."""
+    assert _check(qt, m, 14336, 4096, rows=384) <= TOL
+
+
+def test_gemm_prefill_8192_sampled(cuda):
+    assert _check(O.Q4_K, 8192, 14336, 4096, rows=128) <= TOL
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+def test_gemm_golden_case(cuda, qt):
+    from vllm_webgpu_b200 import ops
+    g = golden(qt)
+    m, n, k = (int(v) for v in g["mm_shape"])
+    y = ops.gemm(torch.from_numpy(g["mm_x"]).cuda(), _wt(g["mm_w"], qt, n, k))
+    assert O.rel_err(y.cpu().numpy(), g["mm_y32"]) <= TOL
+
+
+def test_gemm_matches_gemv_at_m8(cuda):
+    from vllm_webgpu_b200 import ops
+    n, k = 2048, 4096
+    w = _wt(O.make_weights(n, k, O.Q4_K, seed=2), O.Q4_K, n, k)
+    x = torch.randn((8, k), device="cuda").to(torch.bfloat16)
+    a = ops.gemm(x, w, out_dtype=torch.float32)
+    b = ops.gemv(x, w, out_dtype=torch.float32)
+    assert O.rel_err(a.cpu().numpy(), b.cpu().numpy().astype(np.float64)) <= TOL
+
+
+def test_mul_mat_dispatch_and_shape(cuda):
+    from vllm_webgpu_b200 import ops
+    n, k = 512, 4096
+    raw = O.make_weights(n, k, O.Q4_K, seed=3)
+    w = _wt(raw, O.Q4_K, n, k)
+    for m in (1, 8, 9, 40):
+        x = torch.randn((2, m, k), device="cuda").to(torch.bfloat16)
+        y = ops.mul_mat(x, w, out_dtype=torch.float32)
+        assert y.shape == (2, m, n)
+        ref = O.matmul_ref(x.float().reshape(-1, k).cpu().numpy(), raw, O.Q4_K, n, k)
+        assert O.rel_err(y.reshape(-1, n).cpu().numpy(), ref) <= TOL
+
+
+def test_gemm_no_device_timeouts(cuda):
+    from vllm_webgpu_b200 import _lib
+    assert _lib.lib().ggufmm_device_status(1, None) == 0

@@ -1,0 +1,104 @@
+"""Decode GEMV (M <= 8) against the fp32 dequantize-then-matmul oracle.
+
+Gate: max|y - y_ref| / rms(y_ref) <= 2e-3 (the tolerance of the north star)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import gguf_oracle as O
+from tests.helpers import QTYPES, QNAMES, TOL, bf16_round, golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _wt(raw, qt, n, k):
+    from vllm_webgpu_b200.formats import GGUFQuantTensor
+    return GGUFQuantTensor(torch.from_numpy(np.ascontiguousarray(raw).reshape(n, -1)).cuda(), qt, (n, k))
+
+
+def _run(qt, m, n, k, xdtype=torch.bfloat16, ydtype=torch.float32, seed=0):
+    from vllm_webgpu_b200 import ops
+    raw = O.make_weights(n, k, qt, seed=seed)
+    x = O.make_activations(m, k, seed=seed + 1)
+    xt = torch.from_numpy(x).to(xdtype).cuda()
+    y = ops.gemv(xt, _wt(raw, qt, n, k), out_dtype=ydtype)
+    torch.cuda.synchronize()
+    ref = O.matmul_ref(xt.float().cpu().numpy(), raw, qt, n, k)
+    return y.float().cpu().numpy(), ref
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 8])
+def test_gemv_llama_shapes(cuda, qt, m):
+    y, ref = _run(qt, m, 4096, 4096)
+    assert O.rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("n,k", [(14336, 4096), (4096, 14336), (1024, 4096)])
+def test_gemv_layer_shapes_m1(cuda, qt, n, k):
+    y, ref = _run(qt, 1, n, k)
+    assert O.rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("n,k,m", [(1, 2048, 1), (5, 2048, 3), (7, 6144, 2), (13, 18432, 1), (9, 32768, 1),
+                                   (3, 65536, 1)])
+def test_gemv_ragged_and_wide(cuda, qt, n, k, m):
+    """N not a multiple of the row tile; K needing 1, 2 or more segments per thread."""
+    y, ref = _run(qt, m, n, k)
+    assert O.rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("xd", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("yd", [torch.float32, torch.float16, torch.bfloat16])
+def test_gemv_dtypes(cuda, xd, yd):
+    y, ref = _run(O.Q4_K, 2, 2048, 4096, xdtype=xd, ydtype=yd)
+    tol = TOL if yd == torch.float32 else (5e-3 if yd == torch.float16 else 2e-2)
+    assert O.rel_err(y, ref) <= tol
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+def test_gemv_golden_case(cuda, qt):
+    from vllm_webgpu_b200 import ops
+    g = golden(qt)
+    m, n, k = (int(v) for v in g["mm_shape"])
+    if O.row_bytes(qt, k) % 16:
+        pytest.skip("rows not 16-byte multiples")
+    y = ops.gemv(torch.from_numpy(g["mm_x"]).cuda(), _wt(g["mm_w"], qt, n, k))
+    assert O.rel_err(y.cpu().numpy(), g["mm_y32"]) <= TOL
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+def test_gemv_linearity(cuda, qt):
+    """W(a x1 + x2) == a W x1 + W x2 (fp32 activations)."""
+    from vllm_webgpu_b200 import ops
+    n, k = 512, 4096
+    w = _wt(O.make_weights(n, k, qt, seed=9), qt, n, k)
+    rng = np.random.default_rng(4)
+    x1 = torch.from_numpy(rng.standard_normal((1, k), dtype=np.float32)).cuda()
+    x2 = torch.from_numpy(rng.standard_normal((1, k), dtype=np.float32)).cuda()
+    lhs = ops.gemv(2.0 * x1 + x2, w)
+    rhs = 2.0 * ops.gemv(x1, w) + ops.gemv(x2, w)
+    assert O.rel_err(lhs.cpu().numpy(), rhs.cpu().numpy()) <= 1e-4
+
+
+def test_gemv_zero_and_strided_input(cuda):
+    from vllm_webgpu_b200 import ops
+    n, k = 256, 4096
+    raw = O.make_weights(n, k, O.Q4_K, seed=1)
+    w = _wt(raw, O.Q4_K, n, k)
+    z = ops.gemv(torch.zeros((3, k), dtype=torch.bfloat16, device="cuda"), w)
+    assert torch.count_nonzero(z).item() == 0
+    big = torch.randn((4, 2 * k), device="cuda").to(torch.bfloat16)
+    xs = big[:, :k]  # row stride 2K
+    y = ops.gemv(xs, w)
+    ref = O.matmul_ref(xs.float().cpu().numpy(), raw, O.Q4_K, n, k)
+    assert O.rel_err(y.cpu().numpy(), ref) <= TOL
+
+
+def test_gemv_no_device_timeouts(cuda):
+    from vllm_webgpu_b200 import _lib
+    assert _lib.lib().ggufmm_device_status(1, None) == 0

@@ -1,0 +1,205 @@
+// capi.cu -- the extern "C" boundary of libggufmm (declared in include/ggufmm.h).
+//
+// Argument validation happens here, on the host, before anything is enqueued:
+// a failing call launches nothing and returns a negative status. This mirrors
+// the reference's host-side checks (ValueError for bad dimensions in
+// vllm_webgpu/models/llama.py:45-54; FileNotFoundError/RuntimeError for a
+// missing pipeline in vllm_webgpu/webgpu/pipeline.py:25-30).
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ggufmm {
+
+cudaError_t launch_dequant(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype,
+                           cudaStream_t st);
+cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, void* out,
+                              cudaStream_t st);
+cudaError_t launch_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
+                        int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
+cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
+                            int64_t ldy, cudaStream_t st);
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+
+static constexpr int kMaxDev = 64;
+static DevInfo g_dev[kMaxDev];
+static std::once_flag g_dev_once[kMaxDev];
+static int g_dev_major[kMaxDev];
+
+DevInfo device_info(int dev) {
+  if (dev < 0 || dev >= kMaxDev) return DevInfo{};
+  std::call_once(g_dev_once[dev], [dev] {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) g_dev[dev].sms = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess)
+      g_dev[dev].smem_optin = v;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess) g_dev_major[dev] = v;
+  });
+  return g_dev[dev];
+}
+
+static thread_local int t_last_cuda_error = 0;
+
+static int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return GGUFMM_OK;
+  t_last_cuda_error = static_cast<int>(e);
+  return GGUFMM_ERR_CUDA;
+}
+
+static int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  device_info(dev);
+  if (dev >= kMaxDev || g_dev_major[dev] != 10) return GGUFMM_ERR_DEVICE;
+  return GGUFMM_OK;
+}
+
+static int block_of(int qtype) {
+  switch (qtype) {
+    case kQ4_0: case kQ8_0: return 32;
+    case kQ4_K: case kQ6_K: return 256;
+    default: return 0;
+  }
+}
+static int bytes_of(int qtype) {
+  switch (qtype) {
+    case kQ4_0: return 18;
+    case kQ8_0: return 34;
+    case kQ4_K: return 144;
+    case kQ6_K: return 210;
+    default: return 0;
+  }
+}
+static int elem_size(int dtype) {
+  switch (dtype) {
+    case GGUFMM_F32: return 4;
+    case GGUFMM_F16: case GGUFMM_BF16: return 2;
+    default: return 0;
+  }
+}
+static bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+static constexpr int64_t kMaxK = 1 << 20;
+
+static int check_matmul_args(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                             int64_t ldx, const void* y, int y_dtype, int64_t ldy) {
+  if (!q || !x || !y) return GGUFMM_ERR_ARG;
+  if (!block_of(qtype)) return GGUFMM_ERR_QTYPE;
+  if (!elem_size(x_dtype) || !elem_size(y_dtype)) return GGUFMM_ERR_DTYPE;
+  if (n <= 0 || k <= 0 || m <= 0 || k > kMaxK || n > (int64_t(1) << 31) - 1 || m > (int64_t(1) << 31) - 1)
+    return GGUFMM_ERR_SHAPE;
+  if (k % block_of(qtype)) return GGUFMM_ERR_SHAPE;
+  if (ldx < k || ldy < n) return GGUFMM_ERR_SHAPE;
+  return GGUFMM_OK;
+}
+
+}  // namespace ggufmm
+
+using namespace ggufmm;
+
+extern "C" {
+
+int ggufmm_version(void) { return GGUFMM_VERSION; }
+int ggufmm_block_size(int qtype) { return block_of(qtype); }
+int ggufmm_type_size(int qtype) { return bytes_of(qtype); }
+int ggufmm_last_cuda_error(void) { return t_last_cuda_error; }
+
+const char* ggufmm_status_string(int s) {
+  switch (s) {
+    case GGUFMM_OK: return "ok";
+    case GGUFMM_ERR_QTYPE: return "unsupported quantization type";
+    case GGUFMM_ERR_SHAPE: return "invalid shape (K must be a multiple of the block size; M, N, K > 0; ld >= row length)";
+    case GGUFMM_ERR_ALIGN: return "misaligned pointer or row stride";
+    case GGUFMM_ERR_DTYPE: return "unsupported dtype";
+    case GGUFMM_ERR_WORKSPACE: return "workspace missing or too small";
+    case GGUFMM_ERR_CUDA: return "CUDA error";
+    case GGUFMM_ERR_ARG: return "invalid argument";
+    case GGUFMM_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    default: return "unknown status";
+  }
+}
+
+int ggufmm_device_status(int clear, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int a = 0, b = 0;
+  cudaError_t e = gemv_device_error(&a, clear, st);
+  if (e == cudaSuccess) e = gemm_device_error(&b, clear, st);
+  if (e != cudaSuccess) return cuda_status(e);
+  return a | b;
+}
+
+int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
+  if (!q || !out) return GGUFMM_ERR_ARG;
+  if (!block_of(qtype)) return GGUFMM_ERR_QTYPE;
+  if (out_dtype != GGUFMM_F32 && out_dtype != GGUFMM_F16) return GGUFMM_ERR_DTYPE;
+  if (n_rows <= 0 || k <= 0 || k % block_of(qtype) || k > kMaxK) return GGUFMM_ERR_SHAPE;
+  if (!aligned(q, 2) || !aligned(out, 16)) return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  return cuda_status(launch_dequant(q, qtype, n_rows, k, out, out_dtype, static_cast<cudaStream_t>(stream)));
+}
+
+int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                void* y, int y_dtype, int64_t ldy, void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (m > 8) return GGUFMM_ERR_SHAPE;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  if (!aligned(q, 16) || row_bytes % 16 || !aligned(x, 16) || (ldx * elem_size(x_dtype)) % 16 ||
+      !aligned(y, elem_size(y_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  if (row_bytes > 160 * 1024) return GGUFMM_ERR_SHAPE;  // one weight row must fit a shared-memory stage
+  s = check_device();
+  if (s) return s;
+  return cuda_status(launch_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
+                                 static_cast<cudaStream_t>(stream)));
+}
+
+static size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+
+size_t ggufmm_gemm_workspace_size(int qtype, int64_t m, int64_t n, int64_t k) {
+  if (!block_of(qtype) || m <= 0 || n <= 0 || k <= 0 || k % block_of(qtype)) return 0;
+  return round256(static_cast<size_t>(n) * k * 2) + round256(static_cast<size_t>(m) * k * 2);
+}
+
+int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, int64_t ldx,
+                void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  const size_t need = ggufmm_gemm_workspace_size(qtype, m, n, k);
+  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!aligned(q, 2) || !aligned(workspace, 256) || !aligned(y, elem_size(y_dtype)) ||
+      !aligned(x, elem_size(x_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  s = check_device();
+  if (s) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w16 = static_cast<uint8_t*>(workspace);
+  uint8_t* x16 = w16 + round256(static_cast<size_t>(n) * k * 2);
+  cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
+  if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
+  if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st);
+  return cuda_status(e);
+}
+
+int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                   int64_t ldx, void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  const bool gemv_ok = m <= 8 && aligned(q, 16) && row_bytes % 16 == 0 && row_bytes <= 160 * 1024 && aligned(x, 16) &&
+                       (ldx * elem_size(x_dtype)) % 16 == 0;
+  if (gemv_ok) return ggufmm_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, stream);
+  return ggufmm_gemm(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

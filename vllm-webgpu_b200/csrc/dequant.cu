@@ -1,0 +1,212 @@
+// dequant.cu -- GGUF block dequantization on the GPU, bit-identical to
+// gguf-py's numpy dequantizers (gguf quants.py:241-251 Q4_0, 396-401 Q8_0,
+// 504-522 Q4_K, 555-572 Q6_K), plus the fp16 activation cast the tensor-core
+// GEMM consumes.
+//
+// One thread produces 32 consecutive output weights (one Q4_0/Q8_0 block, one
+// Q4_K sub-block, one 32-wide group of a Q6_K superblock). Every product and
+// difference is a separately rounded fp32 op (__fmul_rn / __fsub_rn), in the
+// order gguf-py evaluates them, so no FMA contraction can change a bit.
+// The kernel is HBM-bound on the output write (4 B per weight for fp32).
+#include "common.cuh"
+
+namespace ggufmm {
+
+// Load `NW` 32-bit words starting at a 2-byte-aligned global address.
+template <int NW>
+__device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* w) {
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    uint32_t lo = __ldg(h + 2 * i), hi = __ldg(h + 2 * i + 1);
+    w[i] = lo | (hi << 16);
+  }
+}
+
+__device__ __forceinline__ uint32_t byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xFFu; }
+
+template <int QT>
+__device__ __forceinline__ void dequant32(const uint8_t* row, int unit, float* out);
+
+// Q4_0: d * (nib - 8); byte j: low nibble = elt j, high nibble = elt j+16.
+template <>
+__device__ __forceinline__ void dequant32<kQ4_0>(const uint8_t* row, int unit, float* o) {
+  const uint8_t* b = row + 18 * unit;
+  float d = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(b)));
+  uint32_t w[4];
+  ldg_words_a2<4>(b + 2, w);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    uint32_t v = byte_of(w, j);
+    o[j] = __fmul_rn(d, static_cast<float>(static_cast<int>(v & 15u) - 8));
+    o[j + 16] = __fmul_rn(d, static_cast<float>(static_cast<int>(v >> 4) - 8));
+  }
+}
+
+// Q8_0: q * d.
+template <>
+__device__ __forceinline__ void dequant32<kQ8_0>(const uint8_t* row, int unit, float* o) {
+  const uint8_t* b = row + 34 * unit;
+  float d = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(b)));
+  uint32_t w[8];
+  ldg_words_a2<8>(b + 2, w);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    int q = static_cast<int>(static_cast<int8_t>(byte_of(w, j)));
+    o[j] = __fmul_rn(static_cast<float>(q), d);
+  }
+}
+
+// Q4_K sub-block j of superblock sb: (d*sc_j)*q - (dmin*m_j).
+__device__ __forceinline__ void q4k_scale_min(const uint32_t* s, int j, uint32_t& sc, uint32_t& m) {
+  // s = the 12 scale bytes as 3 little-endian words (bytes 4..15 of the block)
+  if (j < 4) {
+    sc = byte_of(s, j) & 63u;
+    m = byte_of(s, j + 4) & 63u;
+  } else {
+    sc = (byte_of(s, j + 4) & 15u) | ((byte_of(s, j - 4) >> 6) << 4);
+    m = (byte_of(s, j + 4) >> 4) | ((byte_of(s, j) >> 6) << 4);
+  }
+}
+
+template <>
+__device__ __forceinline__ void dequant32<kQ4_K>(const uint8_t* row, int unit, float* o) {
+  const int sb = unit >> 3, j = unit & 7;
+  const uint8_t* b = row + 144 * sb;
+  uint32_t hdr[4];
+  ldg_words_a2<4>(b, hdr);  // d, dmin, 12 scale bytes
+  float d = half_bits_to_float(hdr[0]);
+  float dmin = half_bits_to_float(hdr[0] >> 16);
+  uint32_t sc, m;
+  q4k_scale_min(hdr + 1, j, sc, m);
+  const float dsc = __fmul_rn(d, static_cast<float>(sc));
+  const float dm = __fmul_rn(dmin, static_cast<float>(m));
+  uint32_t w[8];
+  ldg_words_a2<8>(b + 16 + 32 * (j >> 1), w);
+  const int sh = 4 * (j & 1);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    uint32_t q = (byte_of(w, i) >> sh) & 15u;
+    o[i] = __fsub_rn(__fmul_rn(dsc, static_cast<float>(q)), dm);
+  }
+}
+
+// Q6_K group g (0..7) of superblock sb: element e = 32g + c, h = g/4, u = g%4:
+//   q6 = ((ql[h*64 + (u%2)*32 + c] >> 4*(u/2)) & 15) | (((qh[h*32 + c] >> 2u) & 3) << 4)
+//   value = (d * sc[e/16]) * (q6 - 32)
+template <>
+__device__ __forceinline__ void dequant32<kQ6_K>(const uint8_t* row, int unit, float* o) {
+  const int sb = unit >> 3, g = unit & 7, h = g >> 2, u = g & 3;
+  const uint8_t* b = row + 210 * sb;
+  uint32_t ql[8], qh[8];
+  ldg_words_a2<8>(b + h * 64 + (u & 1) * 32, ql);
+  ldg_words_a2<8>(b + 128 + h * 32, qh);
+  const uint16_t scw = __ldg(reinterpret_cast<const uint16_t*>(b + 192 + 2 * g));
+  const float d = half_bits_to_float(__ldg(reinterpret_cast<const uint16_t*>(b + 208)));
+  const float dl0 = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(scw & 0xFF)));
+  const float dl1 = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(scw >> 8)));
+  const int shl = 4 * (u >> 1), shh = 2 * u;
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    int q = static_cast<int>(((byte_of(ql, c) >> shl) & 15u) | (((byte_of(qh, c) >> shh) & 3u) << 4)) - 32;
+    o[c] = __fmul_rn(c < 16 ? dl0 : dl1, static_cast<float>(q));
+  }
+}
+
+template <int QT, int OT>
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ q, int64_t n_units,
+                                                      int units_per_row, int64_t row_bytes,
+                                                      void* __restrict__ out) {
+  const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= n_units) return;
+  const int64_t r = u / units_per_row;
+  const int c = static_cast<int>(u - r * units_per_row);
+  float v[32];
+  dequant32<QT>(q + r * row_bytes, c, v);
+  if (OT == GGUFMM_F32) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + u * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + u * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 h2 = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+        w[j] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      o[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <int QT, int OT>
+static cudaError_t launch_dequant_t(const void* q, int64_t n_rows, int64_t k, void* out, cudaStream_t st) {
+  const int64_t units_per_row = k / 32;
+  const int64_t n_units = n_rows * units_per_row;
+  const int64_t row_bytes = k / QTraits<QT>::kBlock * QTraits<QT>::kBytes;
+  const int threads = 256;
+  const int64_t blocks = (n_units + threads - 1) / threads;
+  dequant_kernel<QT, OT><<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+      static_cast<const uint8_t*>(q), n_units, static_cast<int>(units_per_row), row_bytes, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype,
+                           cudaStream_t st) {
+#define GGUFMM_DQ(QT)                                                                     \
+  case QT:                                                                                \
+    return out_dtype == GGUFMM_F32 ? launch_dequant_t<QT, GGUFMM_F32>(q, n_rows, k, out, st) \
+                                   : launch_dequant_t<QT, GGUFMM_F16>(q, n_rows, k, out, st);
+  switch (qtype) {
+    GGUFMM_DQ(kQ4_0)
+    GGUFMM_DQ(kQ8_0)
+    GGUFMM_DQ(kQ4_K)
+    GGUFMM_DQ(kQ6_K)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef GGUFMM_DQ
+}
+
+// Activation cast x[M, K] (row stride ldx, f32/f16/bf16) -> fp16 [M, K]
+// contiguous, 8 elements per thread. bf16 -> fp16 is exact for |x| in the
+// fp16 normal range; values beyond +-65504 become +-inf.
+template <int XT>
+__global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict__ x, int64_t m, int64_t k,
+                                                         int64_t ldx, __half* __restrict__ out) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  const int64_t total = m * k;
+  if (i >= total) return;
+  const int64_t r = i / k, c = i - r * k;
+  __half tmp[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (c + j < k) {
+      float v;
+      if (XT == GGUFMM_F32) v = static_cast<const float*>(x)[r * ldx + c + j];
+      else if (XT == GGUFMM_F16) v = __half2float(static_cast<const __half*>(x)[r * ldx + c + j]);
+      else v = __bfloat162float(static_cast<const __nv_bfloat16*>(x)[r * ldx + c + j]);
+      tmp[j] = __float2half_rn(v);
+    } else {
+      tmp[j] = __float2half_rn(0.f);
+    }
+  }
+  // k is a multiple of 32, so c..c+7 never straddles a row and out+i is 16-byte aligned.
+  *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<uint4*>(tmp);
+}
+
+cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, void* out,
+                              cudaStream_t st) {
+  const int64_t n8 = (m * k + 7) / 8;
+  const unsigned blocks = static_cast<unsigned>((n8 + 255) / 256);
+  __half* o = static_cast<__half*>(out);
+  if (x_dtype == GGUFMM_F32) cast_x_f16_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  else if (x_dtype == GGUFMM_F16) cast_x_f16_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  else cast_x_f16_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  return cudaGetLastError();
+}
+
+}  // namespace ggufmm

@@ -1,0 +1,266 @@
+// gemm_tc.cu -- prefill / batched GEMM on the sm_100a 5th-generation tensor
+// cores: Y[m, n] = sum_k X[m, k] W[n, k] with fp16 operands (W is the GGUF
+// weight dequantized in fp32 and rounded once to fp16, X the activations cast
+// to fp16) and fp32 accumulation in tensor memory (TMEM).
+//
+// Replaces matmul_quant_mr4.wgsl:77-131 of maci0/vllm-webgpu (one thread per
+// 4x1 output tile, never dispatched) and the token-at-a-time prefill of
+// run_inference.py:323-350.
+//
+// One CTA computes a 128 (weight rows) x BN (tokens) tile; the weight rows are
+// the MMA's M dimension ("swap AB"), so decode-sized token counts still fill
+// the 128-lane datapath. Warp roles (192 threads):
+//   warp 0      TMA producer: 2-D tiled loads (128-byte swizzle) of the W and X
+//               k-blocks into a `kStages`-deep shared-memory ring; completion
+//               via mbarrier transaction counts.
+//   warp 1      allocates TMEM; one elected lane issues tcgen05.mma
+//               (kind::f16, M=128, N=BN, K=16) per 16-wide k-step, commits
+//               each stage back to the producer, and finally the accumulator
+//               to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM (each warp owns the 32
+//               TMEM lanes its warp-in-quad index selects), transpose on the
+//               fly, coalesced stores of Y.
+// No TMA multicast is used anywhere (safe on multi-GPU jobs).
+#include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+
+namespace ggufmm {
+
+constexpr int kTileW = 128;  // weight rows per CTA tile (MMA M)
+constexpr int kBK = 64;      // k elements per stage: 64 fp16 = one 128-byte swizzle row
+
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
+  // K-major operand, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);         // start address
+  d |= static_cast<uint64_t>(1) << 16;                          // leading byte offset (unused for SW128 K-major)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                  // stride byte offset
+  d |= static_cast<uint64_t>(1) << 46;                          // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                          // layout: SWIZZLE_128B
+  return d;
+}
+
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t umma_idesc_f16() {
+  // D = f32 (bits 4-5 = 1), A = B = f16 (0), both K-major, N>>3 at bit 17, M>>4 at bit 24.
+  return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(kTileW >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t kABytes = kTileW * kBK * 2;  // 16 KB
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarOff = STAGES * kStageBytes;
+  static constexpr uint32_t kTotal = kBarOff + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                   void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled tiles need 1024-byte aligned bases
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kTileW, m0 = blockIdx.y * BN;
+  const int nk = (k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        if (!mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1)) break;
+        uint8_t* a_dst = smem + s * L::kStageBytes;
+        uint8_t* b_dst = a_dst + L::kABytes;
+        mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+        tma_load_2d(a_dst, &tmap_w, kb * kBK, n0, &full[s]);
+        tma_load_2d(b_dst, &tmap_x, kb * kBK, m0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16<BN>();
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % STAGES;
+        ok = mbar_wait(&full[s], (kb / STAGES) & 1);
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+        const uint32_t b_addr = a_addr + L::kABytes;
+        const uint64_t adesc = umma_smem_desc(a_addr), bdesc = umma_smem_desc(b_addr);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // advance 16 fp16 = 32 bytes along K inside the swizzle atom
+          umma_f16(tmem_d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+      }
+      umma_commit(accum);  // all MMAs issued so far complete -> accumulator ready
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lanes 32*(warp%4) .. +31 = weight rows
+    const int quad = warp & 3;
+    const bool ok = mbar_wait(accum, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const int nrow = n0 + quad * 32 + lane;
+      const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c0, r);
+        if (nrow < n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int mm = m0 + c0 + j;
+            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(BN) : "memory");
+  }
+}
+
+// ---- host side --------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+// fp16 row-major [rows, k] tensor, box = 64 (k) x box_rows, 128-byte swizzle.
+static bool make_map_f16(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static std::mutex g_gemm_attr_mu;
+static std::set<std::pair<const void*, int>> g_gemm_attr_done;
+
+template <int BN, int STAGES>
+static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
+                                  int ytype, int64_t ldy, cudaStream_t st) {
+  using L = GemmSmem<BN, STAGES>;
+  CUtensorMap mw, mx;
+  if (!make_map_f16(&mw, w16, n, k, kTileW) || !make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
+  auto fn = gemm_tc_kernel<BN, STAGES>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(g_gemm_attr_mu);
+    if (!g_gemm_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::kTotal));
+      if (e != cudaSuccess) return e;
+      g_gemm_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
+    }
+  }
+  dim3 grid(static_cast<unsigned>((n + kTileW - 1) / kTileW), static_cast<unsigned>((m + BN - 1) / BN));
+  fn<<<grid, 192, L::kTotal, st>>>(mw, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
+                                   static_cast<int>(k));
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+
+// Tensor-core GEMM on fp16 operands already in device memory:
+// w16 [n, k], x16 [m, k] (both row-major, 16-byte aligned, k % 8 == 0).
+cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
+                            int64_t ldy, cudaStream_t st) {
+  if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
+  if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
+  if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st);
+  return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st);
+}
+
+}  // namespace ggufmm

@@ -1,0 +1,140 @@
+"""PyTorch-facing operators over libggufmm (CUDA tensors in, CUDA tensors out).
+
+These are the calls the model linear layers make in place of the reference's
+``_dispatch("matmul_quant", [x, W, scales, out], {K, N, USE_QUANT}, ...)``
+(vllm_webgpu/models/base.py:62-100, vllm_webgpu/models/llama.py:276-283).
+Every function launches hand-written sm_100a kernels on the current CUDA
+stream and returns without synchronizing. There is no CPU path: tensors must
+live on a CUDA device and the native library must be present.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .formats import GGUFQuantTensor
+
+_DTYPE_CODE = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+GEMV_MAX_M = 8
+
+
+def _code(dtype: torch.dtype) -> int:
+    if dtype not in _DTYPE_CODE:
+        raise ValueError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16")
+    return _DTYPE_CODE[dtype]
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if t.device.type != "cuda":
+            raise ValueError("libggufmm operates on CUDA tensors only (no CPU fallback)")
+        if t.device != dev:
+            raise ValueError(f"tensors on different devices: {t.device} vs {dev}")
+    return dev
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _as_2d(x: torch.Tensor, k: int) -> torch.Tensor:
+    if x.shape[-1] != k:
+        raise ValueError(f"activation last dim {x.shape[-1]} != K={k}")
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2
+
+
+def _out(x2: torch.Tensor, n: int, out: torch.Tensor | None, out_dtype: torch.dtype | None) -> torch.Tensor:
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype or x2.dtype, device=x2.device)
+    else:
+        if out.dim() != 2 or out.shape[0] != m or out.shape[1] != n or out.stride(1) != 1:
+            raise ValueError(f"out must be a row-major [{m}, {n}] tensor")
+    return out
+
+
+def dequantize(w: GGUFQuantTensor, out_dtype: torch.dtype = torch.float32,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """[N, K] dequantized weights; float32 output is bit-identical to
+    gguf.quants.dequantize (the reference loader's decoder)."""
+    dev = _require_cuda(w.data)
+    n, k = w.shape
+    if out is None:
+        out = torch.empty((n, k), dtype=out_dtype, device=dev)
+    elif out.shape != (n, k) or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous [{n}, {k}] tensor")
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_dequantize(w.data.data_ptr(), w.qtype, n, k, out.data_ptr(),
+                                          _code(out.dtype), _stream(dev))
+    _lib.check(st, "ggufmm_dequantize")
+    return out
+
+
+def gemv(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Decode GEMV, M <= 8 tokens: out[m, n] = sum_k x[m, k] W[n, k]."""
+    dev = _require_cuda(x, w.data)
+    x2 = _as_2d(x, w.k)
+    y = _out(x2, w.n, out, out_dtype)
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemv(w.data.data_ptr(), w.qtype, w.n, w.k, x2.data_ptr(), _code(x2.dtype),
+                                    x2.shape[0], x2.stride(0), y.data_ptr(), _code(y.dtype), y.stride(0),
+                                    _stream(dev))
+    _lib.check(st, "ggufmm_gemv")
+    return y
+
+
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def workspace_for(w: GGUFQuantTensor, m: int) -> torch.Tensor:
+    """A cached per-device scratch buffer large enough for ggufmm_gemm."""
+    need = int(_lib.lib().ggufmm_gemm_workspace_size(w.qtype, m, w.n, w.k))
+    idx = w.data.device.index
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=w.data.device)
+        _workspaces[idx] = ws
+    return ws
+
+
+def gemm(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Tensor-core (tcgen05) GEMM, any M: out[m, n] = sum_k x[m, k] W[n, k]."""
+    dev = _require_cuda(x, w.data)
+    x2 = _as_2d(x, w.k)
+    y = _out(x2, w.n, out, out_dtype)
+    ws = workspace if workspace is not None else workspace_for(w, x2.shape[0])
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemm(w.data.data_ptr(), w.qtype, w.n, w.k, x2.data_ptr(), _code(x2.dtype),
+                                    x2.shape[0], x2.stride(0), y.data_ptr(), _code(y.dtype), y.stride(0),
+                                    ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(st, "ggufmm_gemm")
+    return y
+
+
+def mul_mat(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
+            out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """y = x @ W^T, GEMV for M <= 8 and tensor-core GEMM above.
+
+    Same contract as vLLM's ``fused_mul_mat_gguf(x, qweight, qweight_type)``
+    (vllm/model_executor/layers/quantization/gguf.py:198-230); the leading
+    dimensions of ``x`` are preserved.
+    """
+    lead = x.shape[:-1]
+    x2 = _as_2d(x, w.k)
+    m = x2.shape[0]
+    if m <= GEMV_MAX_M:
+        try:
+            y = gemv(x2, w, out=out, out_dtype=out_dtype)
+        except ValueError:
+            # unaligned operands: the GEMM path has no alignment requirement
+            y = gemm(x2, w, out=out, out_dtype=out_dtype)
+    else:
+        y = gemm(x2, w, out=out, out_dtype=out_dtype)
+    return y.reshape(*lead, w.n)
