@@ -94,7 +94,7 @@ def test_gemv_zero_and_strided_input(cuda):
     assert torch.count_nonzero(z).item() == 0
     big = torch.randn((4, 2 * k), device="cuda").to(torch.bfloat16)
     xs = big[:, :k]  # row stride 2K
-    y = ops.gemv(xs, w)
+    y = ops.gemv(xs, w, out_dtype=torch.float32)
     ref = O.matmul_ref(xs.float().cpu().numpy(), raw, O.Q4_K, n, k)
     assert O.rel_err(y.cpu().numpy(), ref) <= TOL
 

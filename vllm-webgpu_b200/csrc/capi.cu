@@ -19,6 +19,10 @@ cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, 
 cudaError_t launch_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
                         int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
+bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
+cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
+                            int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                             int64_t ldy, cudaStream_t st);
@@ -129,11 +133,12 @@ const char* ggufmm_status_string(int s) {
 
 int ggufmm_device_status(int clear, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   cudaError_t e = gemv_device_error(&a, clear, st);
   if (e == cudaSuccess) e = gemm_device_error(&b, clear, st);
+  if (e == cudaSuccess) e = gemv_mma_device_error(&c, clear, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return a | b;
+  return a | b | c;
 }
 
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
@@ -159,6 +164,11 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   if (row_bytes > 160 * 1024) return GGUFMM_ERR_SHAPE;  // one weight row must fit a shared-memory stage
   s = check_device();
   if (s) return s;
+  // tensor-core GEMV when the shape allows (K a multiple of 256, activations fit
+  // in shared memory), else the CUDA-core streaming GEMV
+  if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype))
+    return cuda_status(launch_gemv_mma(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
+                                       static_cast<cudaStream_t>(stream)));
   return cuda_status(launch_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                  static_cast<cudaStream_t>(stream)));
 }

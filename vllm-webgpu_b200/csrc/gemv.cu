@@ -93,44 +93,58 @@ __device__ __forceinline__ uint32_t byte_to_15(uint32_t w) {
 
 constexpr uint32_t kOne = 0x3F800000u;
 
-// acc += {1 + lo(b)*2^-8 .., 1 + hi(b)*2^-4 ..} . x for the 8 nibbles of w.
-// xl/xh are the activations matching the low / high nibbles of bytes 0..3.
-__device__ __forceinline__ void nib_word_dot(uint32_t w, const float* xl, const float* xh, float2& al,
-                                             float2& ah) {
-  const uint32_t s0 = byte_to_15<0>(w), s1 = byte_to_15<1>(w), s2 = byte_to_15<2>(w), s3 = byte_to_15<3>(w);
-  float2 l01 = make_float2(__uint_as_float((s0 & 0x00078000u) | kOne), __uint_as_float((s1 & 0x00078000u) | kOne));
-  float2 l23 = make_float2(__uint_as_float((s2 & 0x00078000u) | kOne), __uint_as_float((s3 & 0x00078000u) | kOne));
-  float2 h01 = make_float2(__uint_as_float((s0 & 0x00780000u) | kOne), __uint_as_float((s1 & 0x00780000u) | kOne));
-  float2 h23 = make_float2(__uint_as_float((s2 & 0x00780000u) | kOne), __uint_as_float((s3 & 0x00780000u) | kOne));
-  al = __ffma2_rn(l01, make_float2(xl[0], xl[1]), al);
-  al = __ffma2_rn(l23, make_float2(xl[2], xl[3]), al);
-  ah = __ffma2_rn(h01, make_float2(xh[0], xh[1]), ah);
-  ah = __ffma2_rn(h23, make_float2(xh[2], xh[3]), ah);
+// Packed fp32x2 FMA (sm_100 FFMA2), or two scalar FMAs when
+// GGUFMM_GEMV_SCALAR_FMA is defined (kept for A/B instruction-count checks).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+#ifdef GGUFMM_GEMV_SCALAR_FMA
+  return make_float2(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
+#else
+  return __ffma2_rn(a, b, c);
+#endif
 }
 
-// Per-token activation state for one segment.
+__device__ __forceinline__ float2 f2bits(uint32_t a, uint32_t b) {
+  return make_float2(__uint_as_float(a), __uint_as_float(b));
+}
+
+// acc += {1 + lo(b)*2^-8 ..} . xl and {1 + hi(b)*2^-4 ..} . xh for the 8 nibbles
+// of w; xl[0] = x of bytes (0,1), xl[1] = x of bytes (2,3) (same for xh).
+__device__ __forceinline__ void nib_word_dot(uint32_t w, const float2* xl, const float2* xh, float2& al,
+                                             float2& ah) {
+  const uint32_t s0 = byte_to_15<0>(w), s1 = byte_to_15<1>(w), s2 = byte_to_15<2>(w), s3 = byte_to_15<3>(w);
+  al = fma2(f2bits((s0 & 0x00078000u) | kOne, (s1 & 0x00078000u) | kOne), xl[0], al);
+  al = fma2(f2bits((s2 & 0x00078000u) | kOne, (s3 & 0x00078000u) | kOne), xl[1], al);
+  ah = fma2(f2bits((s0 & 0x00780000u) | kOne, (s1 & 0x00780000u) | kOne), xh[0], ah);
+  ah = fma2(f2bits((s2 & 0x00780000u) | kOne, (s3 & 0x00780000u) | kOne), xh[1], ah);
+}
+
+// Per-token activation state for one segment: v[i] = (x[slot 2i], x[slot 2i+1]),
+// slots 0..15 = x[k0..k0+15], slots 16..31 = x[k1..k1+15].
 struct XSeg {
-  float v[32];   // v[0..15] = x[k0..], v[16..31] = x[k1..]
+  float2 v[16];
   float s0, s1;  // sums of the two halves
 };
 
 __device__ __forceinline__ void load_xseg(const void* x, int xtype, int64_t row_off, int k0, int k1, XSeg& xs) {
+  float t[32];
   if (xtype == GGUFMM_BF16) {
-    load_x16<GGUFMM_BF16>(x, row_off + k0, xs.v);
-    load_x16<GGUFMM_BF16>(x, row_off + k1, xs.v + 16);
+    load_x16<GGUFMM_BF16>(x, row_off + k0, t);
+    load_x16<GGUFMM_BF16>(x, row_off + k1, t + 16);
   } else if (xtype == GGUFMM_F16) {
-    load_x16<GGUFMM_F16>(x, row_off + k0, xs.v);
-    load_x16<GGUFMM_F16>(x, row_off + k1, xs.v + 16);
+    load_x16<GGUFMM_F16>(x, row_off + k0, t);
+    load_x16<GGUFMM_F16>(x, row_off + k1, t + 16);
   } else {
-    load_x16<GGUFMM_F32>(x, row_off + k0, xs.v);
-    load_x16<GGUFMM_F32>(x, row_off + k1, xs.v + 16);
+    load_x16<GGUFMM_F32>(x, row_off + k0, t);
+    load_x16<GGUFMM_F32>(x, row_off + k1, t + 16);
   }
   float a = 0.f, b = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    a += xs.v[i];
-    b += xs.v[16 + i];
+    a += t[i];
+    b += t[16 + i];
   }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) xs.v[i] = make_float2(t[2 * i], t[2 * i + 1]);
   xs.s0 = a;
   xs.s1 = b;
 }
@@ -151,28 +165,22 @@ __device__ __forceinline__ void seg_dot_q4k(const uint32_t* base, uint32_t row, 
   const uint4 hdr = *reinterpret_cast<const uint4*>(base + (blk >> 2));
   const uint4 qv = *reinterpret_cast<const uint4*>(base + ((blk + 16u + 32u * c + 16u * (p & 1)) >> 2));
   const float d = half_bits_to_float(hdr.x), dmin = half_bits_to_float(hdr.x >> 16);
-  // 6-bit scales/mins of sub-blocks j0 = 2c, j1 = 2c+1 (gguf quants.py:479-501)
-  uint32_t sc0, m0, sc1, m1;
-  if (c < 2) {
-    const uint32_t sw = hdr.y >> (16 * c), mw = hdr.z >> (16 * c);
-    sc0 = sw & 63u; sc1 = (sw >> 8) & 63u;
-    m0 = mw & 63u;  m1 = (mw >> 8) & 63u;
-  } else {
-    const int sh = 16 * (c - 2);
-    const uint32_t lw = hdr.w >> sh, sw = hdr.y >> sh, mw = hdr.z >> sh;
-    sc0 = (lw & 15u) | (((sw >> 6) & 3u) << 4);
-    m0 = ((lw >> 4) & 15u) | (((mw >> 6) & 3u) << 4);
-    sc1 = ((lw >> 8) & 15u) | (((sw >> 14) & 3u) << 4);
-    m1 = ((lw >> 12) & 15u) | (((mw >> 14) & 3u) << 4);
-  }
-  const float dsc0 = d * static_cast<float>(sc0) * 256.f, dsc1 = d * static_cast<float>(sc1) * 16.f;
-  const float dm0 = dmin * static_cast<float>(m0), dm1 = dmin * static_cast<float>(m1);
+  // 6-bit scales/mins (gguf quants.py:479-501), four sub-blocks per word, branch-free:
+  //   sub-blocks 0..3: sc = s[j] & 63,  m = s[j+4] & 63
+  //   sub-blocks 4..7: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,  m = (s[j+4] >> 4) | (s[j] >> 6) << 4
+  const uint32_t scw = c < 2 ? (hdr.y & 0x3F3F3F3Fu) : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
+  const uint32_t mw = c < 2 ? (hdr.z & 0x3F3F3F3Fu) : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
+  const uint32_t sh = 16u * (c & 1);  // sub-blocks 2c, 2c+1 are bytes (2c&3), (2c&3)+1 of the word
+  const float dsc0 = d * static_cast<float>((scw >> sh) & 0xFFu) * 256.f;
+  const float dsc1 = d * static_cast<float>((scw >> (sh + 8)) & 0xFFu) * 16.f;
+  const float dm0 = dmin * static_cast<float>((mw >> sh) & 0xFFu);
+  const float dm1 = dmin * static_cast<float>((mw >> (sh + 8)) & 0xFFu);
   const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     float2 al = make_float2(-xs[t].s0, 0.f), ah = make_float2(-xs[t].s1, 0.f);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) nib_word_dot(w[i], xs[t].v + 4 * i, xs[t].v + 16 + 4 * i, al, ah);
+    for (int i = 0; i < 4; ++i) nib_word_dot(w[i], xs[t].v + 2 * i, xs[t].v + 8 + 2 * i, al, ah);
     // al = 2^-8 sum q_lo x, ah = 2^-4 sum q_hi x
     out[t] += dsc0 * (al.x + al.y) - dm0 * xs[t].s0 + dsc1 * (ah.x + ah.y) - dm1 * xs[t].s1;
   }
@@ -191,7 +199,7 @@ __device__ __forceinline__ void seg_dot_q40(const uint32_t* base, uint32_t row, 
   for (int t = 0; t < NT; ++t) {
     float2 al = make_float2(-xs[t].s0, 0.f), ah = make_float2(-xs[t].s1, 0.f);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) nib_word_dot(w[i], xs[t].v + 4 * i, xs[t].v + 16 + 4 * i, al, ah);
+    for (int i = 0; i < 4; ++i) nib_word_dot(w[i], xs[t].v + 2 * i, xs[t].v + 8 + 2 * i, al, ah);
     const float qx = 256.f * (al.x + al.y) + 16.f * (ah.x + ah.y);
     out[t] += d * (qx - 8.f * (xs[t].s0 + xs[t].s1));
   }
@@ -214,11 +222,8 @@ __device__ __forceinline__ void seg_dot_q80(const uint32_t* base, uint32_t row, 
     for (int i = 0; i < 8; ++i) {
       const uint32_t s0 = byte_to_15<0>(w[i]), s1 = byte_to_15<1>(w[i]), s2 = byte_to_15<2>(w[i]),
                      s3 = byte_to_15<3>(w[i]);
-      const float* xv = xs[t].v + 4 * i;
-      a = __ffma2_rn(make_float2(__uint_as_float((s0 & 0x007F8000u) | kOne), __uint_as_float((s1 & 0x007F8000u) | kOne)),
-                     make_float2(xv[0], xv[1]), a);
-      a = __ffma2_rn(make_float2(__uint_as_float((s2 & 0x007F8000u) | kOne), __uint_as_float((s3 & 0x007F8000u) | kOne)),
-                     make_float2(xv[2], xv[3]), a);
+      a = fma2(f2bits((s0 & 0x007F8000u) | kOne, (s1 & 0x007F8000u) | kOne), xs[t].v[2 * i], a);
+      a = fma2(f2bits((s2 & 0x007F8000u) | kOne, (s3 & 0x007F8000u) | kOne), xs[t].v[2 * i + 1], a);
     }
     out[t] += d * (256.f * (a.x + a.y) - 128.f * (xs[t].s0 + xs[t].s1));
   }
@@ -258,10 +263,8 @@ __device__ __forceinline__ void seg_dot_q6k(const uint32_t* base, uint32_t row, 
     float2 a0 = make_float2(-xs[t].s0, 0.f), a1 = make_float2(-xs[t].s1, 0.f);
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
-      a0 = __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
-                      make_float2(xs[t].v[j], xs[t].v[j + 1]), a0);
-      a1 = __ffma2_rn(make_float2(__uint_as_float(v[16 + j]), __uint_as_float(v[17 + j])),
-                      make_float2(xs[t].v[16 + j], xs[t].v[17 + j]), a1);
+      a0 = fma2(f2bits(v[j], v[j + 1]), xs[t].v[j >> 1], a0);
+      a1 = fma2(f2bits(v[16 + j], v[17 + j]), xs[t].v[8 + (j >> 1)], a1);
     }
     // a = 2^-6 sum q6 x ; sum (q6-32) x = 64 a - 32 sum x
     out[t] += dl0 * ((a0.x + a0.y) - 0.5f * xs[t].s0) + dl1 * ((a1.x + a1.y) - 0.5f * xs[t].s1);

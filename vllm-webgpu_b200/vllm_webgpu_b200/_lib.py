@@ -10,7 +10,9 @@ from __future__ import annotations
 import ctypes
 import os
 
-_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libggufmm.so")
+# GGUFMM_LIBRARY may point at another build of the same library (e.g. a debug build).
+_LIB_PATH = os.environ.get("GGUFMM_LIBRARY") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "lib", "libggufmm.so")
 
 # status codes (include/ggufmm.h, enum ggufmm_status)
 OK = 0

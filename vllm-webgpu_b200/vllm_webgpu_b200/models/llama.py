@@ -1,0 +1,61 @@
+"""The Llama layer's quantized projections, called the way the reference's
+``LlamaWebGPUModel._transformer_layer`` calls them
+(vllm_webgpu/models/llama.py:276-283 q/k/v, :328-332 o, :343-348 gate/up,
+:355-359 down), each through ``_dispatch("matmul_quant", ...)``.
+
+The reference picks ``USE_QUANT = 0 if q_proj.weight is present`` and so never
+runs its quantized branch (llama.py:258); here the branch is chosen by the
+weight's type, so GGUF blocks always take the quantized kernels.
+Attention, norms and RoPE between the projections are outside this path.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..formats import GGUFQuantTensor
+from .base import BaseB200Model
+
+PROJ = {
+    "q": "self_attn.q_proj.weight", "k": "self_attn.k_proj.weight", "v": "self_attn.v_proj.weight",
+    "o": "self_attn.o_proj.weight", "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight",
+    "down": "mlp.down_proj.weight",
+}
+
+
+class LlamaB200Model(BaseB200Model):
+    """Holds the weights and runs a layer's seven projections."""
+
+    def _w(self, layer: int, proj: str):
+        return self.weights[f"model.layers.{layer}.{PROJ[proj]}"]
+
+    def _linear(self, x: torch.Tensor, w, out: torch.Tensor) -> torch.Tensor:
+        n, k = (w.shape if isinstance(w, GGUFQuantTensor) else tuple(w.shape))
+        use_quant = 1 if isinstance(w, GGUFQuantTensor) else 0
+        self._dispatch("matmul_quant", [x, w, None, out], {"K": k, "N": n, "USE_QUANT": use_quant},
+                       ((n + 255) // 256, 1, 1))
+        return out
+
+    def project_qkv(self, layer: int, normed: torch.Tensor, q_buf, k_buf, v_buf):
+        for buf, p in ((q_buf, "q"), (k_buf, "k"), (v_buf, "v")):
+            self._linear(normed, self._w(layer, p), buf)
+        return q_buf, k_buf, v_buf
+
+    def project_o(self, layer: int, attn_out: torch.Tensor, out: torch.Tensor):
+        return self._linear(attn_out, self._w(layer, "o"), out)
+
+    def project_gate_up(self, layer: int, ffn_normed: torch.Tensor, gate_buf, up_buf):
+        self._linear(ffn_normed, self._w(layer, "gate"), gate_buf)
+        self._linear(ffn_normed, self._w(layer, "up"), up_buf)
+        return gate_buf, up_buf
+
+    def project_down(self, layer: int, ffn_act: torch.Tensor, out: torch.Tensor):
+        return self._linear(ffn_act, self._w(layer, "down"), out)
+
+    def layer_linears(self, layer: int, normed, attn_out, ffn_normed, ffn_act, bufs: dict) -> dict:
+        """All seven projections of one layer into caller-owned ``bufs``
+        (keys q, k, v, o, gate, up, down)."""
+        self.project_qkv(layer, normed, bufs["q"], bufs["k"], bufs["v"])
+        self.project_o(layer, attn_out, bufs["o"])
+        self.project_gate_up(layer, ffn_normed, bufs["gate"], bufs["up"])
+        self.project_down(layer, ffn_act, bufs["down"])
+        return bufs

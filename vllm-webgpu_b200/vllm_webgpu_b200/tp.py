@@ -1,0 +1,77 @@
+"""Tensor-parallel Q4_K SwiGLU FFN over NCCL.
+
+The reference has no multi-GPU path at all: one device, gloo-only distributed
+init, custom all-reduce disabled (vllm_webgpu/platform.py:83-84,112,133-135,
+vllm_webgpu/v1/worker.py:56-59). This module is the B200 addition:
+
+* gate and up are split by OUTPUT rows (each rank owns intermediate/P rows,
+  a row slice of the GGUF byte matrix -- no re-quantization);
+* down is split by INPUT columns over the same intermediate range (a
+  superblock-aligned column slice of the GGUF bytes; 28672/8 = 3584 = 14
+  superblocks);
+* each rank computes silu(x Wg_r^T) * (x Wu_r^T) and its partial
+  y_r = a_r Wd_r^T with the sm_100a kernels, then ONE all-reduce (sum) of the
+  [M, hidden] partials joins the ranks (NCCL over NVLink / NVSwitch).
+
+The matmul callable is injectable so the sharding and the collective can be
+tested on CPU ranks (gloo) against the oracle; on GPUs it is always
+``ops.mul_mat``.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from .formats import QUANT_SIZES, GGUFQuantTensor
+
+
+def shard_range(total: int, rank: int, world: int, align: int) -> tuple[int, int]:
+    """[start, stop) of rank's equal share of ``total``, aligned to ``align``."""
+    if total % world:
+        raise ValueError(f"{total} does not split evenly over {world} ranks")
+    per = total // world
+    if per % align:
+        raise ValueError(f"shard of {per} is not a multiple of the {align}-weight block")
+    return rank * per, (rank + 1) * per
+
+
+def shard_ffn(gate: GGUFQuantTensor, up: GGUFQuantTensor, down: GGUFQuantTensor, rank: int,
+              world: int) -> tuple[GGUFQuantTensor, GGUFQuantTensor, GGUFQuantTensor]:
+    """This rank's gate/up row slices and down column slice (byte slices of the GGUF blocks)."""
+    inter, hidden = gate.shape
+    if up.shape != (inter, hidden) or down.shape != (hidden, inter):
+        raise ValueError(f"inconsistent FFN shapes: gate {gate.shape}, up {up.shape}, down {down.shape}")
+    block = QUANT_SIZES[down.qtype][1]
+    i0, i1 = shard_range(inter, rank, world, block)
+    return gate.rows(i0, i1), up.rows(i0, i1), down.cols(i0, i1)
+
+
+class TensorParallelSwiGLU:
+    """y = down(silu(gate(x)) * up(x)), intermediate dimension split over ranks."""
+
+    def __init__(self, gate: GGUFQuantTensor, up: GGUFQuantTensor, down: GGUFQuantTensor, rank: int = 0,
+                 world: int = 1, group=None, matmul: Callable | None = None, presharded: bool = False,
+                 reduce_dtype: torch.dtype = torch.float32):
+        if presharded:
+            self.gate, self.up, self.down = gate, up, down
+        else:
+            self.gate, self.up, self.down = shard_ffn(gate, up, down, rank, world)
+        self.rank, self.world, self.group = rank, world, group
+        if matmul is None:
+            from .ops import mul_mat
+            matmul = mul_mat
+        self.matmul = matmul
+        self.reduce_dtype = reduce_dtype
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        g = self.matmul(x, self.gate, out_dtype=torch.float32)
+        u = self.matmul(x, self.up, out_dtype=torch.float32)
+        act = torch.nn.functional.silu(g) * u  # fp32 SwiGLU, fed to down in fp32
+        y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
+        if self.world > 1:
+            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+        return y
+
+    __call__ = forward
