@@ -10,25 +10,35 @@
 // instruction per weight, and the unused token columns of the n8 tile are
 // free, so M = 1..8 cost the same.
 //
-// Exactness: GGUF scales vary per 32 (or 16) weights along K, so every
-// sub-block's two k16 MMAs go into a fresh fp32 accumulator and are folded
-// into the running sum with the sub-block's scale:
+// Exactness: GGUF scales vary per 32 (Q6_K: 16) weights along K, so every
+// sub-block's MMAs go into a fresh fp32 accumulator that is folded into the
+// running sum with the sub-block's scale:
 //     y += dsc * acc - (bias * dsc + dmin * m) * sum(x over the sub-block)
-// where acc = sum x * (bias + q) (bias = 1024, or 1032 / 1152 where the
-// format's own offset is folded in). Weights therefore enter the dot product
-// as exact integers and scales in fp32: the result is as accurate as the fp32
-// dequantize-then-matmul, not an fp16-rounded weight.
+// where acc = sum x * (bias + q). Weights enter the dot product as exact
+// integers and scales in fp32, so the result is as accurate as the fp32
+// dequantize-then-matmul (not an fp16-rounded weight).
 //
-// Data movement: each CTA owns row blocks of 16 weight rows. The 16 rows x
-// one K chunk (<= 4096 weights) form a "piece" that one elected thread
-// streams into a shared-memory ring with 1-D bulk TMA copies (one per row,
-// completion on an mbarrier); the row pitch is padded so the 8-byte fragment
-// reads are bank-conflict free. The activations are converted once per CTA
-// into fp16 in shared memory, permuted so every B fragment is one 128-bit
-// load, with per-32 sums for the scale fold. 8 warps split the chunk's
-// 256-weight units; partial 16 x 8 tiles are reduced across warps in shared
-// memory and written by the epilogue.
+// Pipeline (warp-specialised, no block-wide barrier in the steady state):
+//   producer warp   streams "pieces" (16 weight rows x one K chunk of <= 4096
+//                   weights) into a ring of shared-memory stages with 1-D bulk
+//                   TMA copies (one per row, completion on the stage's `full`
+//                   mbarrier); a stage is refilled once every compute warp has
+//                   arrived on its `empty` mbarrier.
+//   compute warps   (W of them) each take every W-th 256-weight unit of a piece
+//                   and keep 16 x 8 partial sums in registers across the chunks
+//                   of a row block; at the end of a row block they park their
+//                   partials in one of two reduction buffers (`rfull`).
+//   epilogue warp   sums the W partials of a row block and writes y, then
+//                   releases the buffer (`rempty`).
+// The activations are converted once per CTA into fp16 in shared memory,
+// permuted within groups of 8 ([0,2,1,3,4,6,5,7]) so every B fragment is one
+// 128-bit load, with per-16/32 sums for the scale fold. fp32 activations are
+// split into fp16 hi + lo columns. Token columns beyond M read column 0 and
+// their results are never stored, so no load is predicated.
+// Every mbarrier wait is bounded (kWaitLimit polls), flags g_device_error and
+// unwinds instead of hanging.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -37,11 +47,11 @@
 
 namespace ggufmm {
 
-constexpr int kMmaWarps = 16;
-constexpr int kMmaThreads = kMmaWarps * 32;
 constexpr int kRowsPerBlock = 16;
 constexpr int kUnitK = 256;         // weights per unit (one K-quant superblock, 8 Q4_0/Q8_0 blocks)
 constexpr int kMaxChunkUnits = 16;  // <= 4096 weights per piece
+constexpr int kRedBufs = 2;
+constexpr int kXsCols = 8;          // columns of the x-sum tables
 
 struct MmaArgs {
   const uint8_t* q;
@@ -65,7 +75,7 @@ struct MmaArgs {
   int stages;
   int64_t nrowblocks;
   int x_pitch;      // smem bytes per column of permuted fp16 x
-  uint32_t x_off, xs_off, red_off, bar_off;
+  uint32_t x_off, xs32_off, xs16_off, red_off, bar_off;
 };
 
 // ---- small PTX helpers ---------------------------------------------------------
@@ -88,6 +98,11 @@ __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uin
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
+__device__ __forceinline__ void mma16816_z(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  const float z[4] = {0.f, 0.f, 0.f, 0.f};
+  mma16816(d, a0, a1, a2, a3, b0, b1, z);
+}
 
 // Load 4 bytes from a 2-byte aligned shared-memory byte offset.
 __device__ __forceinline__ uint32_t lds32_a2(const uint8_t* smem, uint32_t off) {
@@ -102,11 +117,10 @@ __device__ __forceinline__ uint32_t lds16(const uint8_t* smem, uint32_t off) {
 // tot/acc layout (mma C fragment): [0,1] = row g, tokens 2t,2t+1; [2,3] = row g+8.
 __device__ __forceinline__ void fold(float* tot, const float* acc, float dsc_g, float coef_g, float dsc_g8,
                                      float coef_g8, float2 xs) {
-  float2 t01 = __ffma2_rn(make_float2(dsc_g, dsc_g), make_float2(acc[0], acc[1]), make_float2(tot[0], tot[1]));
-  t01 = __ffma2_rn(make_float2(-coef_g, -coef_g), xs, t01);
-  float2 t23 = __ffma2_rn(make_float2(dsc_g8, dsc_g8), make_float2(acc[2], acc[3]), make_float2(tot[2], tot[3]));
-  t23 = __ffma2_rn(make_float2(-coef_g8, -coef_g8), xs, t23);
-  tot[0] = t01.x; tot[1] = t01.y; tot[2] = t23.x; tot[3] = t23.y;
+  tot[0] = fmaf(dsc_g, acc[0], fmaf(-coef_g, xs.x, tot[0]));
+  tot[1] = fmaf(dsc_g, acc[1], fmaf(-coef_g, xs.y, tot[1]));
+  tot[2] = fmaf(dsc_g8, acc[2], fmaf(-coef_g8, xs.x, tot[2]));
+  tot[3] = fmaf(dsc_g8, acc[3], fmaf(-coef_g8, xs.y, tot[3]));
 }
 
 // fp16 pairs (bias + q) of the 4-bit fields of w: lo nibbles of bytes (0,2) / (1,3),
@@ -125,60 +139,52 @@ __device__ __forceinline__ Nib4 nibbles(uint32_t w, uint32_t m0f, uint32_t k6400
 
 // ---- per-format unit processing --------------------------------------------------
 // A "unit" is 256 consecutive weights of a row: one Q4_K / Q6_K superblock or 8
-// Q4_0 / Q8_0 blocks. For every format the activations of sub-block j (32
-// weights, or 16 for Q6_K) are x[32j .. 32j+31] of the unit, and the B
-// fragments are read from the permuted fp16 copy of x.
-//
-// `rg`, `rg8` = smem byte offsets of the unit in rows g and g+8; `xcol` = smem
-// byte offset of this thread's token column at the unit's first k (or ~0u if the
-// column is unused); `xs` = per-32 sums, transposed [k/32][16 cols] floats.
-
+// Q4_0 / Q8_0 blocks; sub-block j of the unit (32 weights, 16 for Q6_K) has the
+// activations x[32j .. 32j+31] of the unit.
 struct UnitCtx {
   const uint8_t* smem;
-  uint32_t rg, rg8;     // unit offsets (rows g and g+8)
-  uint32_t xcol;        // x column offset (bytes) or 0xFFFFFFFF
-  const float* xs;      // &xsT[unit*8][0]
-  int g, t, lane;
+  uint32_t rg, rg8;   // smem byte offsets of the unit in rows g and g+8
+  uint32_t xo;        // smem byte offset of this lane's x column at the unit's first k
+  const float* xs32;  // x sums per 32 weights from the unit's first sub-block: [j][kXsCols]
+  const float* xs16;  // ... per 16 weights (Q6_K only)
+  int t, lane;
 };
 
 __device__ __forceinline__ uint4 ldx128(const UnitCtx& c, uint32_t kofs) {
-  if (c.xcol == 0xFFFFFFFFu) return make_uint4(0, 0, 0, 0);
-  return *reinterpret_cast<const uint4*>(c.smem + c.xcol + 2u * kofs);
+  return *reinterpret_cast<const uint4*>(c.smem + c.xo + 2u * kofs);
 }
 __device__ __forceinline__ uint2 ldx64(const UnitCtx& c, uint32_t kofs) {
-  if (c.xcol == 0xFFFFFFFFu) return make_uint2(0, 0);
-  return *reinterpret_cast<const uint2*>(c.smem + c.xcol + 2u * kofs);
+  return *reinterpret_cast<const uint2*>(c.smem + c.xo + 2u * kofs);
 }
-// Sums of x over 16-weight group j16 of the unit for tokens 2t, 2t+1
-// (xs is transposed: [k/16][16 columns]).
-__device__ __forceinline__ float2 ldxs(const UnitCtx& c, int j16) {
-  return *reinterpret_cast<const float2*>(c.xs + j16 * 16 + 2 * c.t);
+__device__ __forceinline__ float2 xs32(const UnitCtx& c, int j) {
+  return *reinterpret_cast<const float2*>(c.xs32 + j * kXsCols + 2 * c.t);
 }
-// ... over 32-weight sub-block j32.
-__device__ __forceinline__ float2 ldxs32(const UnitCtx& c, int j32) {
-  const float2 a = ldxs(c, 2 * j32), b = ldxs(c, 2 * j32 + 1);
-  return make_float2(a.x + b.x, a.y + b.y);
+__device__ __forceinline__ float2 xs16(const UnitCtx& c, int j) {
+  return *reinterpret_cast<const float2*>(c.xs16 + j * kXsCols + 2 * c.t);
 }
 
-// Q4_K: 8 sub-blocks of 32; chunk c (0..3) = 32 qs bytes at 16+32c, low nibbles ->
-// sub-block 2c, high -> 2c+1. Thread t takes bytes 8t..8t+7 of each chunk.
+// Q4_K: 8 sub-blocks of 32; chunk ch (0..3) = 32 qs bytes at 16+32ch, low nibbles ->
+// sub-block 2ch, high -> 2ch+1. Thread t takes bytes 8t..8t+7 of each chunk and
+// decodes the scales of sub-blocks 2t, 2t+1, shared with the quad by shuffles.
 __device__ __forceinline__ void unit_q4k(const UnitCtx& c, float* tot, uint32_t m0f, uint32_t k6400) {
   const uint4 hg = *reinterpret_cast<const uint4*>(c.smem + c.rg);
   const uint4 hg8 = *reinterpret_cast<const uint4*>(c.smem + c.rg8);
-  // this thread decodes sub-blocks 2t, 2t+1 of both rows
-  float dsc[2][2], coef[2][2];  // [row][which]
+  float sv[8];  // [row][which][dsc, coef]
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const uint4 h = r == 0 ? hg : hg8;
     const float d = half_bits_to_float(h.x), dmin = half_bits_to_float(h.x >> 16);
+    // 6-bit scales/mins (gguf quants.py:479-501), four sub-blocks per word:
+    //   0..3: sc = s[j] & 63,  m = s[j+4] & 63
+    //   4..7: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,  m = (s[j+4] >> 4) | (s[j] >> 6) << 4
     const uint32_t scw = c.t < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
     const uint32_t mw = c.t < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
     const uint32_t sh = 16u * (c.t & 1);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const float ds = d * static_cast<float>((scw >> (sh + 8 * i)) & 0xFFu);
-      dsc[r][i] = ds;
-      coef[r][i] = fmaf(1024.f, ds, dmin * static_cast<float>((mw >> (sh + 8 * i)) & 0xFFu));
+      sv[4 * r + 2 * i] = ds;
+      sv[4 * r + 2 * i + 1] = fmaf(1024.f, ds, dmin * static_cast<float>((mw >> (sh + 8 * i)) & 0xFFu));
     }
   }
 #pragma unroll
@@ -186,26 +192,20 @@ __device__ __forceinline__ void unit_q4k(const UnitCtx& c, float* tot, uint32_t 
     const int src = (c.lane & ~3) | ch;
     float s[8];
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        s[4 * r + 2 * i] = __shfl_sync(0xFFFFFFFFu, dsc[r][i], src);
-        s[4 * r + 2 * i + 1] = __shfl_sync(0xFFFFFFFFu, coef[r][i], src);
-      }
+    for (int i = 0; i < 8; ++i) s[i] = __shfl_sync(0xFFFFFFFFu, sv[i], src);
     const uint2 wg = *reinterpret_cast<const uint2*>(c.smem + c.rg + 16u + 32u * ch + 8u * c.t);
     const uint2 wg8 = *reinterpret_cast<const uint2*>(c.smem + c.rg8 + 16u + 32u * ch + 8u * c.t);
     const uint4 xl = ldx128(c, 64u * ch + 8u * c.t);
     const uint4 xh = ldx128(c, 64u * ch + 32u + 8u * c.t);
     const Nib4 a0 = nibbles(wg.x, m0f, k6400), a1 = nibbles(wg8.x, m0f, k6400);
     const Nib4 b0 = nibbles(wg.y, m0f, k6400), b1 = nibbles(wg8.y, m0f, k6400);
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
     float accl[4], acch[4];
-    mma16816(accl, a0.l02, a1.l02, a0.l13, a1.l13, xl.x, xl.y, z);
+    mma16816_z(accl, a0.l02, a1.l02, a0.l13, a1.l13, xl.x, xl.y);
     mma16816(accl, b0.l02, b1.l02, b0.l13, b1.l13, xl.z, xl.w, accl);
-    mma16816(acch, a0.h02, a1.h02, a0.h13, a1.h13, xh.x, xh.y, z);
+    mma16816_z(acch, a0.h02, a1.h02, a0.h13, a1.h13, xh.x, xh.y);
     mma16816(acch, b0.h02, b1.h02, b0.h13, b1.h13, xh.z, xh.w, acch);
-    fold(tot, accl, s[0], s[1], s[4], s[5], ldxs32(c, 2 * ch));
-    fold(tot + 4, acch, s[2], s[3], s[6], s[7], ldxs32(c, 2 * ch + 1));
+    fold(tot, accl, s[0], s[1], s[4], s[5], xs32(c, 2 * ch));
+    fold(tot + 4, acch, s[2], s[3], s[6], s[7], xs32(c, 2 * ch + 1));
   }
 }
 
@@ -220,11 +220,10 @@ __device__ __forceinline__ void unit_q40(const UnitCtx& c, float* tot, uint32_t 
     const uint2 xl = ldx64(c, 32u * b + 4u * c.t);
     const uint2 xh = ldx64(c, 32u * b + 16u + 4u * c.t);
     const Nib4 a = nibbles(wg, m0f, k6400), a8 = nibbles(wg8, m0f, k6400);
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
     float acc[4];
-    mma16816(acc, a.l02, a8.l02, a.l13, a8.l13, xl.x, xl.y, z);
+    mma16816_z(acc, a.l02, a8.l02, a.l13, a8.l13, xl.x, xl.y);
     mma16816(acc, a.h02, a8.h02, a.h13, a8.h13, xh.x, xh.y, acc);
-    fold(tot + 4 * (b & 1), acc, dg, 1032.f * dg, dg8, 1032.f * dg8, ldxs32(c, b));
+    fold(tot + 4 * (b & 1), acc, dg, 1032.f * dg, dg8, 1032.f * dg8, xs32(c, b));
   }
 }
 
@@ -240,13 +239,12 @@ __device__ __forceinline__ void unit_q80(const UnitCtx& c, float* tot) {
     const uint32_t v0 = lds32_a2(c.smem, og8 + 2u + 4u * c.t), v1 = lds32_a2(c.smem, og8 + 18u + 4u * c.t);
     const uint2 x0 = ldx64(c, 32u * b + 4u * c.t);
     const uint2 x1 = ldx64(c, 32u * b + 16u + 4u * c.t);
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
     float acc[4];
-    mma16816(acc, lop_and_xor(w0, mff, kx), lop_and_xor(v0, mff, kx), lop_and_xor(w0 >> 8, mff, kx),
-             lop_and_xor(v0 >> 8, mff, kx), x0.x, x0.y, z);
+    mma16816_z(acc, lop_and_xor(w0, mff, kx), lop_and_xor(v0, mff, kx), lop_and_xor(w0 >> 8, mff, kx),
+               lop_and_xor(v0 >> 8, mff, kx), x0.x, x0.y);
     mma16816(acc, lop_and_xor(w1, mff, kx), lop_and_xor(v1, mff, kx), lop_and_xor(w1 >> 8, mff, kx),
              lop_and_xor(v1 >> 8, mff, kx), x1.x, x1.y, acc);
-    fold(tot + 4 * (b & 1), acc, dg, 1152.f * dg, dg8, 1152.f * dg8, ldxs32(c, b));
+    fold(tot + 4 * (b & 1), acc, dg, 1152.f * dg, dg8, 1152.f * dg8, xs32(c, b));
   }
 }
 
@@ -263,7 +261,7 @@ __device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, uint32_t 
     const int h = grp >> 2, u = grp & 3;
     const uint32_t qlo = 64u * h + 32u * (u & 1), qho = 128u + 32u * h;
     const int shl = 4 * (u >> 1), shh = 2 * u;
-    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t scg = lds16(c.smem, c.rg + 192u + 2u * grp), scg8 = lds16(c.smem, c.rg8 + 192u + 2u * grp);
 #pragma unroll
     for (int s = 0; s < 2; ++s) {  // 16-element scale group 2*grp + s
       const uint32_t cc = 16u * s + 4u * c.t;
@@ -276,12 +274,10 @@ __device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, uint32_t 
       const uint32_t a3 = lop_and_or(lg8 >> 8, m0f, lop_and_or(hg8 >> 4, m30, k6400));
       const uint2 xb = ldx64(c, 32u * grp + cc);
       float acc[4];
-      mma16816(acc, a0, a1, a2, a3, xb.x, xb.y, z);
-      const int sg = 2 * grp + s;
-      const float sc_g = static_cast<float>(static_cast<int8_t>(lds16(c.smem, c.rg + 192u + (sg & ~1)) >> (8 * (sg & 1))));
-      const float sc_g8 = static_cast<float>(static_cast<int8_t>(lds16(c.smem, c.rg8 + 192u + (sg & ~1)) >> (8 * (sg & 1))));
-      const float dl = dg * sc_g, dl8 = dg8 * sc_g8;
-      fold(tot + 4 * s, acc, dl, 1056.f * dl, dl8, 1056.f * dl8, ldxs(c, sg));  // value = dl*(q6-32), bias 1024+32
+      mma16816_z(acc, a0, a1, a2, a3, xb.x, xb.y);
+      const float dl = dg * static_cast<float>(static_cast<int8_t>(scg >> (8 * s)));
+      const float dl8 = dg8 * static_cast<float>(static_cast<int8_t>(scg8 >> (8 * s)));
+      fold(tot + 4 * s, acc, dl, 1056.f * dl, dl8, 1056.f * dl8, xs16(c, 2 * grp + s));  // bias 1024 + 32
     }
   }
 }
@@ -298,43 +294,40 @@ __device__ __forceinline__ void process_unit(const UnitCtx& c, float* tot) {
 // ---- the kernel ---------------------------------------------------------------------
 __device__ __forceinline__ uint32_t perm8(uint32_t e) { return (e & 4u) | ((e & 1u) << 1) | ((e >> 1) & 1u); }
 
-template <int QT>
-__global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaArgs a) {
+// W compute warps + 1 producer warp + 1 epilogue warp.
+template <int QT, int W>
+__global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  constexpr int kThreads = (W + 2) * 32;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.bar_off);
-  float* xsT = reinterpret_cast<float*>(smem + a.xs_off);
-  float* red = reinterpret_cast<float*>(smem + a.red_off);
+  uint64_t* empty = full + a.stages;
+  uint64_t* rfull = empty + a.stages;
+  uint64_t* rempty = rfull + kRedBufs;
+  float* xs32t = reinterpret_cast<float*>(smem + a.xs32_off);
+  float* xs16t = reinterpret_cast<float*>(smem + a.xs16_off);
+  float* red = reinterpret_cast<float*>(smem + a.red_off);  // [kRedBufs][W][16 rows][8 cols]
   const int64_t my_blocks = a.nrowblocks > blockIdx.x ? (a.nrowblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t total_pieces = my_blocks * a.nchunks;
+  const int total_units = a.k / kUnitK;
 
   if (tid == 0) {
-    for (int s = 0; s < a.stages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    for (int b = 0; b < kRedBufs; ++b) {
+      mbar_init(&rfull[b], W);
+      mbar_init(&rempty[b], 1);
+    }
     fence_mbar_init();
   }
-  __syncthreads();
 
-  // piece p -> (row block, chunk); rows of the piece are copied one bulk copy each
-  auto issue = [&](int64_t p, int s) {
-    const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
-    const int ch = static_cast<int>(p % a.nchunks);
-    const int64_t r0 = rb * kRowsPerBlock;
-    const int nr = static_cast<int>((a.n - r0) < kRowsPerBlock ? (a.n - r0) : kRowsPerBlock);
-    const int units = min(a.chunk_units, a.k / kUnitK - ch * a.chunk_units);
-    const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
-    mbar_arrive_expect_tx(&full[s], bytes * nr);
-    uint8_t* dst = smem + s * a.stage_bytes;
-    const uint8_t* src = a.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
-    for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
-  };
-  if (tid == 0) {
-    for (int s = 0; s < a.stages && s < total_pieces; ++s) issue(s, s);
-  }
-
-  // activations -> permuted fp16 [cols][k] (+ per-16 sums, transposed [k/16][16])
+  // activations -> permuted fp16 [cols][k]; sums per 16 / 32 weights, [k/16][8] / [k/32][8]
   {
     const int groups = a.k / 8;  // 8 consecutive k per task
-    for (int task = tid; task < a.m * groups; task += kMmaThreads) {
+    const int nparts = a.xtype == GGUFMM_F32 ? 2 : 1;
+    for (int task = tid; task < a.m * groups; task += kThreads) {
       const int tok = task / groups, k0 = (task - tok * groups) * 8;
       float v[8];
       if (a.xtype == GGUFMM_F32) {
@@ -356,80 +349,116 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaArgs 
           }
         }
       }
-      const int nparts = a.xtype == GGUFMM_F32 ? 2 : 1;
       for (int part = 0; part < nparts; ++part) {
         __half hv[8];
         float s = 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const __half hi = __float2half_rn(v[e]);
-          const __half h = part == 0 ? hi : __float2half_rn(v[e] - __half2float(hi));
-          hv[perm8(e)] = h;
-          s += __half2float(h);
+          const __half hh = part == 0 ? hi : __float2half_rn(v[e] - __half2float(hi));
+          hv[perm8(e)] = hh;
+          s += __half2float(hh);
         }
         const int col = tok + part * a.m;
         *reinterpret_cast<uint4*>(smem + a.x_off + col * a.x_pitch + 2 * k0) = *reinterpret_cast<uint4*>(hv);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);  // 16-weight group = two adjacent tasks
-        if ((task & 1) == 0) xsT[(k0 / 16) * 16 + col] = s;
+        s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);  // 16 weights = two adjacent tasks
+        if (QT == kQ6_K && (task & 1) == 0) xs16t[(k0 / 16) * kXsCols + col] = s;
+        s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);  // 32 weights = four adjacent tasks
+        if ((task & 3) == 0) xs32t[(k0 / 32) * kXsCols + col] = s;
       }
     }
-    // zero the xs entries of unused columns
-    for (int i = tid; i < (a.k / 16) * 16; i += kMmaThreads)
-      if ((i & 15) >= a.cols) xsT[i] = 0.f;
   }
   __syncthreads();
 
-  const uint32_t xcol = g < a.cols ? a.x_off + g * a.x_pitch : 0xFFFFFFFFu;
-  float tot[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // two independent fold chains
-  int64_t p = 0;
-  for (int64_t blk = 0; blk < my_blocks; ++blk) {
-    const int64_t rb = blockIdx.x + blk * gridDim.x;
-    for (int ch = 0; ch < a.nchunks; ++ch, ++p) {
-      const int s = static_cast<int>(p % a.stages);
-      const bool ok = mbar_wait(&full[s], static_cast<uint32_t>((p / a.stages) & 1));
-      if (!__syncthreads_and(ok)) {  // a bounded wait gave up (flag set): drain copies in flight, unwind
-        if (tid == 0)
-          for (int64_t q = p; q < p + a.stages && q < total_pieces; ++q)
-            mbar_wait(&full[q % a.stages], static_cast<uint32_t>((q / a.stages) & 1));
-        return;
+  if (warp == W) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      for (int64_t p = 0; p < total_pieces; ++p) {
+        const int s = static_cast<int>(p % a.stages);
+        if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
+        const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
+        const int ch = static_cast<int>(p % a.nchunks);
+        const int64_t r0 = rb * kRowsPerBlock;
+        const int nr = static_cast<int>((a.n - r0) < kRowsPerBlock ? (a.n - r0) : kRowsPerBlock);
+        const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
+        const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
+        mbar_arrive_expect_tx(&full[s], bytes * nr);
+        uint8_t* dst = smem + s * a.stage_bytes;
+        const uint8_t* src = a.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
+        for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
       }
-      const int units = min(a.chunk_units, a.k / kUnitK - ch * a.chunk_units);
-      const uint32_t sbase = static_cast<uint32_t>(s * a.stage_bytes);
-      for (int u = warp; u < units; u += kMmaWarps) {
-        UnitCtx c;
-        c.smem = smem;
-        c.rg = sbase + g * a.row_pitch + u * a.unit_bytes;
-        c.rg8 = c.rg + 8 * a.row_pitch;
-        const int ku = (ch * a.chunk_units + u) * kUnitK;
-        c.xcol = xcol == 0xFFFFFFFFu ? xcol : xcol + 2u * ku;
-        c.xs = xsT + (ku / 16) * 16;
-        c.g = g; c.t = t; c.lane = lane;
-        process_unit<QT>(c, tot);
-      }
-      __syncthreads();  // stage s consumed by every warp
-      if (tid == 0 && p + a.stages < total_pieces) issue(p + a.stages, s);
     }
-    // cross-warp reduction of the 16 x cols tile, then store
-    float* rw = red + warp * (kRowsPerBlock * 8);
-    *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(tot[0] + tot[4], tot[1] + tot[5]);
-    *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(tot[2] + tot[6], tot[3] + tot[7]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) tot[i] = 0.f;
-    __syncthreads();
-    if (tid < kRowsPerBlock * a.m) {
-      const int row = tid / a.m, tok = tid - row * a.m;
-      const int64_t n_idx = rb * kRowsPerBlock + row;
-      if (n_idx < a.n) {
+  } else if (warp == W + 1) {
+    // ---------------- epilogue ----------------
+    for (int64_t blk = 0; blk < my_blocks; ++blk) {
+      const int b = static_cast<int>(blk & 1);
+      if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
+      const int64_t rb = blockIdx.x + blk * gridDim.x;
+      const float* rbuf = red + b * (W * kRowsPerBlock * 8);
+      for (int i = lane; i < kRowsPerBlock * a.m; i += 32) {
+        const int row = i / a.m, tok = i - row * a.m;
+        const int64_t n_idx = rb * kRowsPerBlock + row;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kMmaWarps; ++w) {
-          v += red[w * (kRowsPerBlock * 8) + row * 8 + tok];
-          if (a.cols > a.m) v += red[w * (kRowsPerBlock * 8) + row * 8 + tok + a.m];
+        for (int w = 0; w < W; ++w) {
+          v += rbuf[(w * kRowsPerBlock + row) * 8 + tok];
+          if (a.cols > a.m) v += rbuf[(w * kRowsPerBlock + row) * 8 + tok + a.m];
         }
-        store_y_rt(a.y, a.ytype, tok * a.ldy + n_idx, v);
+        if (n_idx < a.n) store_y_rt(a.y, a.ytype, tok * a.ldy + n_idx, v);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[b]);
     }
-    __syncthreads();
+  } else {
+    // ---------------- compute ----------------
+    const uint32_t xcol = a.x_off + (g < a.cols ? g : 0) * a.x_pitch;
+    float tot[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // two independent fold chains
+    int64_t p = 0;
+    bool ok = true;
+    for (int64_t blk = 0; blk < my_blocks && ok; ++blk) {
+      for (int ch = 0; ch < a.nchunks; ++ch, ++p) {
+        const int s = static_cast<int>(p % a.stages);
+        if (!mbar_wait(&full[s], static_cast<uint32_t>((p / a.stages) & 1))) {
+          ok = false;
+          break;
+        }
+        const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
+        const uint32_t sbase = static_cast<uint32_t>(s * a.stage_bytes) + g * a.row_pitch;
+        for (int u = warp; u < units; u += W) {
+          const int ku = (ch * a.chunk_units + u) * kUnitK;
+          UnitCtx c;
+          c.smem = smem;
+          c.rg = sbase + u * a.unit_bytes;
+          c.rg8 = c.rg + 8 * a.row_pitch;
+          c.xo = xcol + 2u * ku;
+          c.xs32 = xs32t + (ku / 32) * kXsCols;
+          c.xs16 = xs16t + (ku / 16) * kXsCols;
+          c.t = t;
+          c.lane = lane;
+          process_unit<QT>(c, tot);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
+      }
+      if (!ok) break;
+      // row block complete: park the partial 16 x 8 tile for the epilogue
+      const int b = static_cast<int>(blk & 1);
+      if (blk >= kRedBufs && !mbar_wait(&rempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
+      float* rw = red + b * (W * kRowsPerBlock * 8) + warp * (kRowsPerBlock * 8);
+      *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(tot[0] + tot[4], tot[1] + tot[5]);
+      *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(tot[2] + tot[6], tot[3] + tot[7]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot[i] = 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfull[b]);
+    }
+  }
+  __syncthreads();
+  // A bounded wait may have given up (g_device_error is set): make sure no copy
+  // of this CTA is still in flight before it exits.
+  if (warp == W && lane == 0) {
+    for (int64_t q = total_pieces - a.stages; q < total_pieces; ++q)
+      if (q >= 0) mbar_wait(&full[q % a.stages], static_cast<uint32_t>((q / a.stages) & 1));
   }
 }
 
@@ -453,8 +482,18 @@ static int unit_bytes_of(int qt) {
   }
 }
 
+// Compute warps per CTA (8 by default; GGUFMM_GEMV_WARPS=4|16 for tuning).
+static int compute_warps() {
+  static const int w = [] {
+    const char* e = std::getenv("GGUFMM_GEMV_WARPS");
+    const int v = e ? std::atoi(e) : 8;
+    return v == 16 ? 16 : (v == 4 ? 4 : 8);
+  }();
+  return w;
+}
+
 // Whether the tensor-core GEMV handles this problem; fills the launch plan.
-static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_budget, MmaArgs& a) {
+static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_budget, int W, MmaArgs& a) {
   a.unit_bytes = unit_bytes_of(qt);
   if (!a.unit_bytes || k % kUnitK || m < 1 || m > 8) return false;
   a.cols = xtype == GGUFMM_F32 ? 2 * m : m;
@@ -472,15 +511,17 @@ static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_bu
   a.stage_bytes = kRowsPerBlock * a.row_pitch;
   a.x_pitch = static_cast<int>(2 * k + 64);
   const int x_bytes = a.cols * a.x_pitch;
-  const int xs_bytes = static_cast<int>(k / 16) * 16 * 4;
-  const int red_bytes = kMmaWarps * kRowsPerBlock * 8 * 4;
-  const int fixed = x_bytes + xs_bytes + red_bytes + 8 * 8 + 64;
-  int stages = std::min(4, (smem_budget - fixed) / a.stage_bytes);
+  const int xs32_bytes = static_cast<int>(k / 32) * kXsCols * 4;
+  const int xs16_bytes = qt == kQ6_K ? static_cast<int>(k / 16) * kXsCols * 4 : 0;
+  const int red_bytes = kRedBufs * W * kRowsPerBlock * 8 * 4;
+  const int fixed = x_bytes + xs32_bytes + xs16_bytes + red_bytes + 16 * 8 + 64;
+  const int stages = std::min(6, (smem_budget - fixed) / a.stage_bytes);
   if (stages < 2) return false;
   a.stages = stages;
   a.x_off = static_cast<uint32_t>(stages * a.stage_bytes);
-  a.xs_off = a.x_off + x_bytes;
-  a.red_off = a.xs_off + xs_bytes;
+  a.xs32_off = a.x_off + x_bytes;
+  a.xs16_off = a.xs32_off + xs32_bytes;
+  a.red_off = a.xs16_off + xs16_bytes;
   a.bar_off = (a.red_off + red_bytes + 7) / 8 * 8;
   a.nrowblocks = (n + kRowsPerBlock - 1) / kRowsPerBlock;
   return true;
@@ -491,13 +532,13 @@ bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const DevInfo di = device_info(dev);
-  return plan_mma(qtype, n, k, m, xtype, std::min(di.smem_optin, 227 * 1024), a);
+  return plan_mma(qtype, n, k, m, xtype, std::min(di.smem_optin, 227 * 1024), compute_warps(), a);
 }
 
-template <int QT>
+template <int QT, int W>
 static cudaError_t launch_mma_t(MmaArgs& a, int dev, const DevInfo& di, cudaStream_t st) {
-  auto fn = gemv_mma_kernel<QT>;
-  const int smem = static_cast<int>(a.bar_off + 8 * a.stages);
+  auto fn = gemv_mma_kernel<QT, W>;
+  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs));
   {
     std::lock_guard<std::mutex> lk(g_mma_attr_mu);
     if (!g_mma_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
@@ -508,8 +549,15 @@ static cudaError_t launch_mma_t(MmaArgs& a, int dev, const DevInfo& di, cudaStre
     }
   }
   const int64_t grid = std::min<int64_t>(a.nrowblocks, di.sms);
-  fn<<<static_cast<unsigned>(grid), kMmaThreads, smem, st>>>(a);
+  fn<<<static_cast<unsigned>(grid), (W + 2) * 32, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int QT>
+static cudaError_t launch_mma_q(MmaArgs& a, int W, int dev, const DevInfo& di, cudaStream_t st) {
+  if (W == 16) return launch_mma_t<QT, 16>(a, dev, di, st);
+  if (W == 4) return launch_mma_t<QT, 4>(a, dev, di, st);
+  return launch_mma_t<QT, 8>(a, dev, di, st);
 }
 
 cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
@@ -518,8 +566,9 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const DevInfo di = device_info(dev);
+  const int W = compute_warps();
   MmaArgs a{};
-  if (!plan_mma(qtype, n, k, static_cast<int>(m), xtype, std::min(di.smem_optin, 227 * 1024), a))
+  if (!plan_mma(qtype, n, k, static_cast<int>(m), xtype, std::min(di.smem_optin, 227 * 1024), W, a))
     return cudaErrorInvalidValue;
   a.q = static_cast<const uint8_t*>(q);
   a.n = n;
@@ -533,10 +582,10 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
   a.ytype = ytype;
   a.ldy = ldy;
   switch (qtype) {
-    case kQ4_K: return launch_mma_t<kQ4_K>(a, dev, di, st);
-    case kQ4_0: return launch_mma_t<kQ4_0>(a, dev, di, st);
-    case kQ8_0: return launch_mma_t<kQ8_0>(a, dev, di, st);
-    case kQ6_K: return launch_mma_t<kQ6_K>(a, dev, di, st);
+    case kQ4_K: return launch_mma_q<kQ4_K>(a, W, dev, di, st);
+    case kQ4_0: return launch_mma_q<kQ4_0>(a, W, dev, di, st);
+    case kQ8_0: return launch_mma_q<kQ8_0>(a, W, dev, di, st);
+    case kQ6_K: return launch_mma_q<kQ6_K>(a, W, dev, di, st);
     default: return cudaErrorInvalidValue;
   }
 }
