@@ -135,6 +135,29 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k,
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * ggufmm_gemm without a caller-provided workspace, for callers that cannot
+ * allocate device memory (for example a host whose own pool owns the GPU's
+ * memory and offers no allocator across the FFI, or code that must not
+ * allocate once it is serving). This entry point has no counterpart in the
+ * reference.
+ *
+ * Its scratch is a library-owned __device__ array of
+ * GGUFMM_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps until
+ * the process exits. A problem needing more than that (N*K*2 + M*K*2 bytes,
+ * each rounded up to 256) returns GGUFMM_ERR_WORKSPACE and launches nothing.
+ * The first call on a device looks up the array's address with that device
+ * current; make it before any stream capture. All calls share the array:
+ * calls that can overlap on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller. No cudaMalloc/cudaFree is made.
+ * Same arguments, results and error gate as ggufmm_gemm.
+ */
+#define GGUFMM_NOALLOC_SCRATCH_BYTES (64u << 20) /* 64 MiB */
+
+int ggufmm_gemm_noalloc(const void* q, int qtype, int64_t n, int64_t k,
+                        const void* x, int x_dtype, int64_t m, int64_t ldx,
+                        void* y, int y_dtype, int64_t ldy, void* stream);
+
+/*
  * y = x @ W^T choosing the kernel by M (GEMV for M <= 8, GEMM otherwise), the
  * way vLLM's GGUF linear method picks between its GEMV and GEMM kernels
  * (vllm/model_executor/layers/quantization/gguf.py:198-230). The workspace

@@ -42,6 +42,7 @@ SIGNATURES = {
     "ggufmm_gemm_workspace_size": (_SZ, [_I, _I64, _I64, _I64]),
     "ggufmm_gemm": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
     "ggufmm_mul_mat": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
+    "ggufmm_gemm_noalloc": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
 }
 
 
