@@ -4,19 +4,22 @@
 //   y[m, n] = sum_k x[m, k] W[n, k]
 //
 // Why tensor cores for a GEMV: the cost of a quantized GEMV at HBM speed is
-// the per-weight decode work, not the multiply. On mma.sync.m16n8k16 the
-// decode of two 4-bit quants is ONE lop3 ((w >> s) & 0x000F000F | 0x64006400
-// is the fp16 pair 1024+q0, 1024+q1, exact), the multiply is 1/8 of an
-// instruction per weight, and the unused token columns of the n8 tile are
-// free, so M = 1..8 cost the same.
+// the per-weight decode work, not the multiply. On mma.sync.m16n8k16 a pair of
+// 4-bit quants becomes an fp16 operand with ONE lop3: (w >> s) & 0x000F000F is
+// the pair q0 * 2^-24, q2 * 2^-24 as fp16 subnormals, exact (Q4_K high nibbles
+// are used unshifted, & 0x00F000F0 = 16 q * 2^-24). The multiply is 1/8 of an
+// instruction per weight and the unused token columns of the n8 tile are free,
+// so M = 1..8 cost the same.
 //
 // Exactness: GGUF scales vary per 32 (Q6_K: 16) weights along K, so every
-// sub-block's MMAs go into a fresh fp32 accumulator that is folded into the
-// running sum with the sub-block's scale:
-//     y += dsc * acc - (bias * dsc + dmin * m) * sum(x over the sub-block)
-// where acc = sum x * (bias + q). Weights enter the dot product as exact
-// integers and scales in fp32, so the result is as accurate as the fp32
-// dequantize-then-matmul (not an fp16-rounded weight).
+// scale group's MMAs go into a fresh fp32 accumulator that is folded into the
+// running sum with the group's scale (2^24 folded in): tot += dsc * acc. The
+// group's offset / min part, coef_j * sum(x over group j) (Q4_K: dmin m_j,
+// Q4_0: 8 d, Q8_0: 128 d, Q6_K: 32 d sc_j), is a small matrix product of its
+// own and also runs on the tensor core (bf16 hi/lo splits, accumulated over the
+// row block). Weights enter as exact integers and scales in fp32, so the result
+// is as accurate as the fp32 dequantize-then-matmul (not an fp16-rounded
+// weight).
 //
 // Pipeline (warp-specialised, no block-wide barrier in the steady state):
 //   producer warp   streams "pieces" (16 weight rows x one K chunk of <= 4096
@@ -51,7 +54,6 @@ constexpr int kRowsPerBlock = 16;
 constexpr int kUnitK = 256;         // weights per unit (one K-quant superblock, 8 Q4_0/Q8_0 blocks)
 constexpr int kMaxChunkUnits = 16;  // <= 4096 weights per piece
 constexpr int kRedBufs = 2;
-constexpr int kXsCols = 8;          // columns of the x-sum tables
 
 struct MmaArgs {
   const uint8_t* q;
@@ -75,7 +77,7 @@ struct MmaArgs {
   int stages;
   int64_t nrowblocks;
   int x_pitch;      // smem bytes per column of permuted fp16 x
-  uint32_t x_off, xs32_off, xs16_off, red_off, bar_off;
+  uint32_t x_off, xsb_off, xsb_lo, red_off, bar_off;  // xsb: bf16 x-sum slots, lo part at +xsb_lo
 };
 
 // ---- small PTX helpers ---------------------------------------------------------
@@ -113,18 +115,8 @@ __device__ __forceinline__ uint32_t lds16(const uint8_t* smem, uint32_t off) {
   return *reinterpret_cast<const uint16_t*>(smem + off);
 }
 
-// Running sum fold for one sub-block: tot += dsc * acc - coef * xs.
-// tot/acc layout (mma C fragment): [0,1] = row g, tokens 2t,2t+1; [2,3] = row g+8.
-__device__ __forceinline__ void fold(float* tot, const float* acc, float dsc_g, float coef_g, float dsc_g8,
-                                     float coef_g8, float2 xs) {
-  tot[0] = fmaf(dsc_g, acc[0], fmaf(-coef_g, xs.x, tot[0]));
-  tot[1] = fmaf(dsc_g, acc[1], fmaf(-coef_g, xs.y, tot[1]));
-  tot[2] = fmaf(dsc_g8, acc[2], fmaf(-coef_g8, xs.x, tot[2]));
-  tot[3] = fmaf(dsc_g8, acc[3], fmaf(-coef_g8, xs.y, tot[3]));
-}
-
-// fp16 pairs (bias + q) of the 4-bit fields of w: lo nibbles of bytes (0,2) / (1,3),
-// hi nibbles of bytes (0,2) / (1,3).
+// fp16 pairs of the 4-bit fields of w (or-ed with k, 0 here: fp16 subnormals q * 2^-24):
+// lo nibbles of bytes (0,2) / (1,3), hi nibbles of bytes (0,2) / (1,3).
 struct Nib4 {
   uint32_t l02, l13, h02, h13;
 };
@@ -139,14 +131,19 @@ __device__ __forceinline__ Nib4 nibbles(uint32_t w, uint32_t m0f, uint32_t k6400
 
 // ---- per-format unit processing --------------------------------------------------
 // A "unit" is 256 consecutive weights of a row: one Q4_K / Q6_K superblock or 8
-// Q4_0 / Q8_0 blocks; sub-block j of the unit (32 weights, 16 for Q6_K) has the
-// activations x[32j .. 32j+31] of the unit.
+// Q4_0 / Q8_0 blocks. Its scale groups (8 sub-blocks of 32, or 16 groups of 16
+// for Q6_K) each get a fresh MMA accumulator folded with tot += dsc * acc. The
+// offset / min part of every group, coef_j * sum(x over group j), is itself a small
+// matrix product: coef [16 rows x 16 group slots] times x-sums [16 slots x 8
+// columns]. It runs on the tensor core too (bf16 hi/lo splits of both operands,
+// three MMAs, accurate to ~2^-16), accumulating into `cm` over the whole row
+// block; the row block's result is tot - cm.
 struct UnitCtx {
   const uint8_t* smem;
-  uint32_t rg, rg8;   // smem byte offsets of the unit in rows g and g+8
-  uint32_t xo;        // smem byte offset of this lane's x column at the unit's first k
-  const float* xs32;  // x sums per 32 weights from the unit's first sub-block: [j][kXsCols]
-  const float* xs16;  // ... per 16 weights (Q6_K only)
+  uint32_t rg, rg8;  // smem byte offsets of the unit in rows g and g+8
+  uint32_t xo;       // smem byte offset of this lane's x column at the unit's first k
+  uint32_t xsh;      // smem byte offset of this lane's (unit, column, t) x-sum slots, bf16 hi part
+  uint32_t xsl_add;  // + this = lo part
   int t, lane;
 };
 
@@ -156,20 +153,59 @@ __device__ __forceinline__ uint4 ldx128(const UnitCtx& c, uint32_t kofs) {
 __device__ __forceinline__ uint2 ldx64(const UnitCtx& c, uint32_t kofs) {
   return *reinterpret_cast<const uint2*>(c.smem + c.xo + 2u * kofs);
 }
-__device__ __forceinline__ float2 xs32(const UnitCtx& c, int j) {
-  return *reinterpret_cast<const float2*>(c.xs32 + j * kXsCols + 2 * c.t);
+
+__device__ __forceinline__ void mma_bf16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ float2 xs16(const UnitCtx& c, int j) {
-  return *reinterpret_cast<const float2*>(c.xs16 + j * kXsCols + 2 * c.t);
+
+// bf16x2 hi / lo split of (a, b): a = hi.x + lo.x to ~2^-16 relative.
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// cm += coef . xsums for the unit. coef pairs: (row g, slots 2t,2t+1), (row g+8, ..),
+// (row g, slots 2t+8,2t+9), (row g+8, ..); zero where a format has 8 groups.
+__device__ __forceinline__ void coef_mma(const UnitCtx& c, float* cm, float2 cg, float2 cg8, float2 cg_hi,
+                                         float2 cg8_hi) {
+  uint32_t a0h, a0l, a1h, a1l, a2h, a2l, a3h, a3l;
+  split2(cg.x, cg.y, a0h, a0l);
+  split2(cg8.x, cg8.y, a1h, a1l);
+  split2(cg_hi.x, cg_hi.y, a2h, a2l);
+  split2(cg8_hi.x, cg8_hi.y, a3h, a3l);
+  const uint2 bh = *reinterpret_cast<const uint2*>(c.smem + c.xsh);
+  const uint2 bl = *reinterpret_cast<const uint2*>(c.smem + c.xsh + c.xsl_add);
+  mma_bf16(cm, a0h, a1h, a2h, a3h, bh.x, bh.y);
+  mma_bf16(cm, a0h, a1h, a2h, a3h, bl.x, bl.y);
+  mma_bf16(cm, a0l, a1l, a2l, a3l, bh.x, bh.y);
+}
+
+// tot += d * acc (rows g -> [0,1], g+8 -> [2,3])
+__device__ __forceinline__ void fold_d(float* tot, const float* acc, float d_g, float d_g8) {
+  tot[0] = fmaf(d_g, acc[0], tot[0]);
+  tot[1] = fmaf(d_g, acc[1], tot[1]);
+  tot[2] = fmaf(d_g8, acc[2], tot[2]);
+  tot[3] = fmaf(d_g8, acc[3], tot[3]);
 }
 
 // Q4_K: 8 sub-blocks of 32; chunk ch (0..3) = 32 qs bytes at 16+32ch, low nibbles ->
-// sub-block 2ch, high -> 2ch+1. Thread t takes bytes 8t..8t+7 of each chunk and
-// decodes the scales of sub-blocks 2t, 2t+1, shared with the quad by shuffles.
-__device__ __forceinline__ void unit_q4k(const UnitCtx& c, float* tot, uint32_t m0f, uint32_t k6400) {
+// sub-block 2ch, high -> 2ch+1. Thread t takes bytes 8t..8t+7 of each chunk. Low
+// nibbles enter the MMA as q * 2^-24, high nibbles unshifted as 16 q * 2^-24. Thread t
+// decodes the scales of sub-blocks 2t, 2t+1 and shares the dsc values with its quad.
+__device__ __forceinline__ void unit_q4k(const UnitCtx& c, float* tot, float* cm) {
+  const uint32_t m0f = 0x000F000Fu, mf0 = 0x00F000F0u, k6400 = 0u;  // quants as fp16 subnormals q*2^-24
   const uint4 hg = *reinterpret_cast<const uint4*>(c.smem + c.rg);
   const uint4 hg8 = *reinterpret_cast<const uint4*>(c.smem + c.rg8);
-  float sv[8];  // [row][which][dsc, coef]
+  float sv[4];    // [row][lo dsc, hi dsc/16]
+  float2 cf[2];   // [row] (coef of sub-block 2t, coef of 2t+1)
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const uint4 h = r == 0 ? hg : hg8;
@@ -177,45 +213,63 @@ __device__ __forceinline__ void unit_q4k(const UnitCtx& c, float* tot, uint32_t 
     // 6-bit scales/mins (gguf quants.py:479-501), four sub-blocks per word:
     //   0..3: sc = s[j] & 63,  m = s[j+4] & 63
     //   4..7: sc = (s[j+4] & 15) | (s[j-4] >> 6) << 4,  m = (s[j+4] >> 4) | (s[j] >> 6) << 4
-    const uint32_t scw = c.t < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
-    const uint32_t mw = c.t < 2 ? (h.z & 0x3F3F3F3Fu) : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+    // (branch-free: lanes of a warp differ in t)
+    const uint32_t hi_sel = 0u - static_cast<uint32_t>(c.t >> 1);  // all ones for t >= 2
+    const uint32_t scw = ((h.y & 0x3F3F3F3Fu) & ~hi_sel) | (((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)) & hi_sel);
+    const uint32_t mw = ((h.z & 0x3F3F3F3Fu) & ~hi_sel) | ((((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) & hi_sel);
     const uint32_t sh = 16u * (c.t & 1);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float ds = d * static_cast<float>((scw >> (sh + 8 * i)) & 0xFFu);
-      sv[4 * r + 2 * i] = ds;
-      sv[4 * r + 2 * i + 1] = fmaf(1024.f, ds, dmin * static_cast<float>((mw >> (sh + 8 * i)) & 0xFFu));
-    }
+    const float dlo = d * static_cast<float>((scw >> sh) & 0xFFu);
+    const float dhi = d * static_cast<float>((scw >> (sh + 8)) & 0xFFu);
+    // lows: acc = 2^-24 sum x q, highs (unshifted) acc = 2^-20 sum x q; min term dmin m xs
+    sv[2 * r] = dlo * 16777216.f;
+    sv[2 * r + 1] = dhi * 1048576.f;
+    cf[r] = make_float2(dmin * static_cast<float>((mw >> sh) & 0xFFu), dmin * static_cast<float>((mw >> (sh + 8)) & 0xFFu));
   }
+  coef_mma(c, cm, cf[0], cf[1], make_float2(0.f, 0.f), make_float2(0.f, 0.f));
 #pragma unroll
   for (int ch = 0; ch < 4; ++ch) {
     const int src = (c.lane & ~3) | ch;
-    float s[8];
+    float s[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s[i] = __shfl_sync(0xFFFFFFFFu, sv[i], src);
+    for (int i = 0; i < 4; ++i) s[i] = __shfl_sync(0xFFFFFFFFu, sv[i], src);
     const uint2 wg = *reinterpret_cast<const uint2*>(c.smem + c.rg + 16u + 32u * ch + 8u * c.t);
     const uint2 wg8 = *reinterpret_cast<const uint2*>(c.smem + c.rg8 + 16u + 32u * ch + 8u * c.t);
     const uint4 xl = ldx128(c, 64u * ch + 8u * c.t);
     const uint4 xh = ldx128(c, 64u * ch + 32u + 8u * c.t);
-    const Nib4 a0 = nibbles(wg.x, m0f, k6400), a1 = nibbles(wg8.x, m0f, k6400);
-    const Nib4 b0 = nibbles(wg.y, m0f, k6400), b1 = nibbles(wg8.y, m0f, k6400);
+    const uint32_t g0 = wg.x, g1 = wg.y, h0 = wg8.x, h1 = wg8.y;
+    const uint32_t g0s = g0 >> 8, g1s = g1 >> 8, h0s = h0 >> 8, h1s = h1 >> 8;
     float accl[4], acch[4];
-    mma16816_z(accl, a0.l02, a1.l02, a0.l13, a1.l13, xl.x, xl.y);
-    mma16816(accl, b0.l02, b1.l02, b0.l13, b1.l13, xl.z, xl.w, accl);
-    mma16816_z(acch, a0.h02, a1.h02, a0.h13, a1.h13, xh.x, xh.y);
-    mma16816(acch, b0.h02, b1.h02, b0.h13, b1.h13, xh.z, xh.w, acch);
-    fold(tot, accl, s[0], s[1], s[4], s[5], xs32(c, 2 * ch));
-    fold(tot + 4, acch, s[2], s[3], s[6], s[7], xs32(c, 2 * ch + 1));
+    mma16816_z(accl, lop_and_or(g0, m0f, k6400), lop_and_or(h0, m0f, k6400), lop_and_or(g0s, m0f, k6400),
+               lop_and_or(h0s, m0f, k6400), xl.x, xl.y);
+    mma16816(accl, lop_and_or(g1, m0f, k6400), lop_and_or(h1, m0f, k6400), lop_and_or(g1s, m0f, k6400),
+             lop_and_or(h1s, m0f, k6400), xl.z, xl.w, accl);
+    mma16816_z(acch, lop_and_or(g0, mf0, k6400), lop_and_or(h0, mf0, k6400), lop_and_or(g0s, mf0, k6400),
+               lop_and_or(h0s, mf0, k6400), xh.x, xh.y);
+    mma16816(acch, lop_and_or(g1, mf0, k6400), lop_and_or(h1, mf0, k6400), lop_and_or(g1s, mf0, k6400),
+             lop_and_or(h1s, mf0, k6400), xh.z, xh.w, acch);
+    fold_d(tot, accl, s[0], s[2]);
+    fold_d(tot + 4, acch, s[1], s[3]);
   }
 }
 
 // Q4_0: 8 blocks of 18 bytes (fp16 d + 16 nibble bytes; byte i: low nibble ->
-// x[i], high -> x[16+i]); value d*(q-8). Thread t takes bytes 4t..4t+3.
-__device__ __forceinline__ void unit_q40(const UnitCtx& c, float* tot, uint32_t m0f, uint32_t k6400) {
+// x[i], high -> x[16+i]); value d*(q-8), q entered as q*2^-24. Thread t takes
+// bytes 4t..4t+3 of every block.
+__device__ __forceinline__ void unit_q40(const UnitCtx& c, float* tot, float* cm) {
+  const uint32_t m0f = 0x000F000Fu, k6400 = 0u;
+  {
+    const uint32_t o = 36u * c.t;  // blocks 2t, 2t+1
+    const float2 cg = make_float2(8.f * half_bits_to_float(lds16(c.smem, c.rg + o)),
+                                  8.f * half_bits_to_float(lds16(c.smem, c.rg + o + 18u)));
+    const float2 cg8 = make_float2(8.f * half_bits_to_float(lds16(c.smem, c.rg8 + o)),
+                                   8.f * half_bits_to_float(lds16(c.smem, c.rg8 + o + 18u)));
+    coef_mma(c, cm, cg, cg8, make_float2(0.f, 0.f), make_float2(0.f, 0.f));
+  }
 #pragma unroll
   for (int b = 0; b < 8; ++b) {
     const uint32_t og = c.rg + 18u * b, og8 = c.rg8 + 18u * b;
-    const float dg = half_bits_to_float(lds16(c.smem, og)), dg8 = half_bits_to_float(lds16(c.smem, og8));
+    const float dg = 16777216.f * half_bits_to_float(lds16(c.smem, og));
+    const float dg8 = 16777216.f * half_bits_to_float(lds16(c.smem, og8));
     const uint32_t wg = lds32_a2(c.smem, og + 2u + 4u * c.t), wg8 = lds32_a2(c.smem, og8 + 2u + 4u * c.t);
     const uint2 xl = ldx64(c, 32u * b + 4u * c.t);
     const uint2 xh = ldx64(c, 32u * b + 16u + 4u * c.t);
@@ -223,18 +277,28 @@ __device__ __forceinline__ void unit_q40(const UnitCtx& c, float* tot, uint32_t 
     float acc[4];
     mma16816_z(acc, a.l02, a8.l02, a.l13, a8.l13, xl.x, xl.y);
     mma16816(acc, a.h02, a8.h02, a.h13, a8.h13, xh.x, xh.y, acc);
-    fold(tot + 4 * (b & 1), acc, dg, 1032.f * dg, dg8, 1032.f * dg8, xs32(c, b));
+    fold_d(tot + 4 * (b & 1), acc, dg, dg8);
   }
 }
 
-// Q8_0: 8 blocks of 34 bytes (fp16 d + 32 int8); q+128 as fp16 (1152 + q).
-// Thread t takes bytes 4t..4t+3 (k16 step 0) and 16+4t.. (step 1) of each block.
-__device__ __forceinline__ void unit_q80(const UnitCtx& c, float* tot) {
-  const uint32_t mff = 0x00FF00FFu, kx = 0x64806480u;  // (w & 0x00FF00FF) ^ 0x64806480 = 0x64.. | (byte ^ 0x80)
+// Q8_0: 8 blocks of 34 bytes (fp16 d + 32 int8); u = q+128 enters as u*2^-24,
+// value d*q = d*u - 128 d. Thread t takes bytes 4t..4t+3 (k16 step 0) and
+// 16+4t.. (step 1) of each block.
+__device__ __forceinline__ void unit_q80(const UnitCtx& c, float* tot, float* cm) {
+  const uint32_t mff = 0x00FF00FFu, kx = 0x00800080u;  // (w & 0x00FF00FF) ^ 0x00800080 = byte ^ 0x80
+  {
+    const uint32_t o = 68u * c.t;  // blocks 2t, 2t+1
+    const float2 cg = make_float2(128.f * half_bits_to_float(lds16(c.smem, c.rg + o)),
+                                  128.f * half_bits_to_float(lds16(c.smem, c.rg + o + 34u)));
+    const float2 cg8 = make_float2(128.f * half_bits_to_float(lds16(c.smem, c.rg8 + o)),
+                                   128.f * half_bits_to_float(lds16(c.smem, c.rg8 + o + 34u)));
+    coef_mma(c, cm, cg, cg8, make_float2(0.f, 0.f), make_float2(0.f, 0.f));
+  }
 #pragma unroll
   for (int b = 0; b < 8; ++b) {
     const uint32_t og = c.rg + 34u * b, og8 = c.rg8 + 34u * b;
-    const float dg = half_bits_to_float(lds16(c.smem, og)), dg8 = half_bits_to_float(lds16(c.smem, og8));
+    const float dg = 16777216.f * half_bits_to_float(lds16(c.smem, og));
+    const float dg8 = 16777216.f * half_bits_to_float(lds16(c.smem, og8));
     const uint32_t w0 = lds32_a2(c.smem, og + 2u + 4u * c.t), w1 = lds32_a2(c.smem, og + 18u + 4u * c.t);
     const uint32_t v0 = lds32_a2(c.smem, og8 + 2u + 4u * c.t), v1 = lds32_a2(c.smem, og8 + 18u + 4u * c.t);
     const uint2 x0 = ldx64(c, 32u * b + 4u * c.t);
@@ -244,18 +308,28 @@ __device__ __forceinline__ void unit_q80(const UnitCtx& c, float* tot) {
                lop_and_xor(v0 >> 8, mff, kx), x0.x, x0.y);
     mma16816(acc, lop_and_xor(w1, mff, kx), lop_and_xor(v1, mff, kx), lop_and_xor(w1 >> 8, mff, kx),
              lop_and_xor(v1 >> 8, mff, kx), x1.x, x1.y, acc);
-    fold(tot + 4 * (b & 1), acc, dg, 1152.f * dg, dg8, 1152.f * dg8, xs32(c, b));
+    fold_d(tot + 4 * (b & 1), acc, dg, dg8);
   }
 }
 
 // Q6_K: element e = 128h + 32u + cc (h = 0..1, u = 0..3, cc = 0..31):
 // q6 = (ql[64h + 32(u&1) + cc] >> 4(u>>1)) & 15 | ((qh[128 + 32h + cc] >> 2u) & 3) << 4,
-// value = (d * sc[e/16]) * (q6 - 32). One k16 step = one 16-weight scale group;
-// thread t takes elements cc = 16s + 4t .. +3.
-__device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, uint32_t k6400) {
+// value = (d * sc[e/16]) * (q6 - 32), q6 entered as q6*2^-24. One k16 step = one
+// 16-weight scale group; thread t takes elements cc = 16s + 4t .. +3.
+__device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, float* cm) {
+  const uint32_t k6400 = 0u, m0f = 0x000F000Fu, m30 = 0x00300030u;
   const float dg = half_bits_to_float(lds16(c.smem, c.rg + 208u));
   const float dg8 = half_bits_to_float(lds16(c.smem, c.rg8 + 208u));
-  const uint32_t m0f = 0x000F000Fu, m30 = 0x00300030u;
+  {
+    // groups 2t, 2t+1 (slots 2t, 2t+1) and 2t+8, 2t+9 (slots 2t+8, 2t+9)
+    const uint32_t o = 192u + 2u * c.t;
+    const uint32_t s0 = lds16(c.smem, c.rg + o), s1 = lds16(c.smem, c.rg + o + 8u);
+    const uint32_t r0 = lds16(c.smem, c.rg8 + o), r1 = lds16(c.smem, c.rg8 + o + 8u);
+    auto sc = [](uint32_t v, int i) { return static_cast<float>(static_cast<int8_t>(v >> (8 * i))); };
+    const float kg = 32.f * dg, kg8 = 32.f * dg8;
+    coef_mma(c, cm, make_float2(kg * sc(s0, 0), kg * sc(s0, 1)), make_float2(kg8 * sc(r0, 0), kg8 * sc(r0, 1)),
+             make_float2(kg * sc(s1, 0), kg * sc(s1, 1)), make_float2(kg8 * sc(r1, 0), kg8 * sc(r1, 1)));
+  }
 #pragma unroll
   for (int grp = 0; grp < 8; ++grp) {  // 32-element group = 128h + 32u
     const int h = grp >> 2, u = grp & 3;
@@ -267,7 +341,7 @@ __device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, uint32_t 
       const uint32_t cc = 16u * s + 4u * c.t;
       const uint32_t lg = lds32_a2(c.smem, c.rg + qlo + cc) >> shl, lg8 = lds32_a2(c.smem, c.rg8 + qlo + cc) >> shl;
       const uint32_t hg = lds32_a2(c.smem, c.rg + qho + cc) >> shh, hg8 = lds32_a2(c.smem, c.rg8 + qho + cc) >> shh;
-      // bytes (0,2) and (1,3): (nibble | hi2 << 4) | 0x6400 = fp16 1024 + q6
+      // bytes (0,2) and (1,3): nibble | hi2 << 4 = q6 as an fp16 subnormal (q6 * 2^-24)
       const uint32_t a0 = lop_and_or(lg, m0f, lop_and_or(hg << 4, m30, k6400));
       const uint32_t a2 = lop_and_or(lg >> 8, m0f, lop_and_or(hg >> 4, m30, k6400));
       const uint32_t a1 = lop_and_or(lg8, m0f, lop_and_or(hg8 << 4, m30, k6400));
@@ -275,20 +349,19 @@ __device__ __forceinline__ void unit_q6k(const UnitCtx& c, float* tot, uint32_t 
       const uint2 xb = ldx64(c, 32u * grp + cc);
       float acc[4];
       mma16816_z(acc, a0, a1, a2, a3, xb.x, xb.y);
-      const float dl = dg * static_cast<float>(static_cast<int8_t>(scg >> (8 * s)));
-      const float dl8 = dg8 * static_cast<float>(static_cast<int8_t>(scg8 >> (8 * s)));
-      fold(tot + 4 * s, acc, dl, 1056.f * dl, dl8, 1056.f * dl8, xs16(c, 2 * grp + s));  // bias 1024 + 32
+      const float dl = 16777216.f * dg * static_cast<float>(static_cast<int8_t>(scg >> (8 * s)));
+      const float dl8 = 16777216.f * dg8 * static_cast<float>(static_cast<int8_t>(scg8 >> (8 * s)));
+      fold_d(tot + 4 * s, acc, dl, dl8);
     }
   }
 }
 
 template <int QT>
-__device__ __forceinline__ void process_unit(const UnitCtx& c, float* tot) {
-  const uint32_t m0f = 0x000F000Fu, k6400 = 0x64006400u;
-  if (QT == kQ4_K) unit_q4k(c, tot, m0f, k6400);
-  else if (QT == kQ4_0) unit_q40(c, tot, m0f, k6400);
-  else if (QT == kQ8_0) unit_q80(c, tot);
-  else unit_q6k(c, tot, k6400);
+__device__ __forceinline__ void process_unit(const UnitCtx& c, float* tot, float* cm) {
+  if (QT == kQ4_K) unit_q4k(c, tot, cm);
+  else if (QT == kQ4_0) unit_q40(c, tot, cm);
+  else if (QT == kQ8_0) unit_q80(c, tot, cm);
+  else unit_q6k(c, tot, cm);
 }
 
 // ---- the kernel ---------------------------------------------------------------------
@@ -304,8 +377,7 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
   uint64_t* empty = full + a.stages;
   uint64_t* rfull = empty + a.stages;
   uint64_t* rempty = rfull + kRedBufs;
-  float* xs32t = reinterpret_cast<float*>(smem + a.xs32_off);
-  float* xs16t = reinterpret_cast<float*>(smem + a.xs16_off);
+  __nv_bfloat16* xsb = reinterpret_cast<__nv_bfloat16*>(smem + a.xsb_off);  // [unit][col][t][4] hi, then lo
   float* red = reinterpret_cast<float*>(smem + a.red_off);  // [kRedBufs][W][16 rows][8 cols]
   const int64_t my_blocks = a.nrowblocks > blockIdx.x ? (a.nrowblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t total_pieces = my_blocks * a.nchunks;
@@ -322,6 +394,29 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
     }
     fence_mbar_init();
   }
+
+  // piece p -> (row block, chunk); 16 rows, one bulk copy per row into the padded stage
+  auto issue = [&](int64_t p, int s) {
+    const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
+    const int ch = static_cast<int>(p % a.nchunks);
+    const int64_t r0 = rb * kRowsPerBlock;
+    const int nr = static_cast<int>((a.n - r0) < kRowsPerBlock ? (a.n - r0) : kRowsPerBlock);
+    const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
+    const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
+    mbar_arrive_expect_tx(&full[s], bytes * nr);
+    uint8_t* dst = smem + s * a.stage_bytes;
+    const uint8_t* src = a.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
+    for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
+  };
+  // Weights are read-only inputs: start streaming them before anything else
+  // (and, under programmatic dependent launch, before the previous kernel on the
+  // stream has finished).
+  if (tid == 0)
+    for (int s = 0; s < a.stages && s < total_pieces; ++s) issue(s, s);
+  // Let the next kernel on the stream begin its own prologue as SMs free up.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // The activations (and the outputs) may belong to the previous kernel: wait for it.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // activations -> permuted fp16 [cols][k]; sums per 16 / 32 weights, [k/16][8] / [k/32][8]
   {
@@ -361,10 +456,25 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
         }
         const int col = tok + part * a.m;
         *reinterpret_cast<uint4*>(smem + a.x_off + col * a.x_pitch + 2 * k0) = *reinterpret_cast<uint4*>(hv);
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);  // 16 weights = two adjacent tasks
-        if (QT == kQ6_K && (task & 1) == 0) xs16t[(k0 / 16) * kXsCols + col] = s;
-        s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);  // 32 weights = four adjacent tasks
-        if ((task & 3) == 0) xs32t[(k0 / 32) * kXsCols + col] = s;
+        // x sums per scale group (16 weights = 2 tasks for Q6_K, 32 = 4 tasks otherwise),
+        // stored as bf16 hi + lo in the B-fragment slot order of coef_mma:
+        // slot j -> position 4 * ((j & 7) >> 1) + (j & 1) + 2 * (j >> 3)
+        s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+        if (QT != kQ6_K) s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+        const int gsz = QT == kQ6_K ? 16 : 32;
+        if ((task & (gsz / 8 - 1)) == 0) {
+          const int unit = k0 / kUnitK, j = (k0 % kUnitK) / gsz;
+          __nv_bfloat16* e = xsb + (unit * a.cols + col) * 16;
+          const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(s - __bfloat162float(hi));
+          const int pos = 4 * ((j & 7) >> 1) + (j & 1) + 2 * (j >> 3);
+          e[pos] = hi;
+          e[pos + a.xsb_lo / 2] = lo;
+          if (QT != kQ6_K) {  // 8 groups per unit: slots 8..15 are zero
+            e[pos + 2] = __float2bfloat16_rn(0.f);
+            e[pos + 2 + a.xsb_lo / 2] = __float2bfloat16_rn(0.f);
+          }
+        }
       }
     }
   }
@@ -373,19 +483,10 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
   if (warp == W) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      for (int64_t p = 0; p < total_pieces; ++p) {
+      for (int64_t p = a.stages; p < total_pieces; ++p) {  // pieces < stages: issued in the prologue
         const int s = static_cast<int>(p % a.stages);
         if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
-        const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
-        const int ch = static_cast<int>(p % a.nchunks);
-        const int64_t r0 = rb * kRowsPerBlock;
-        const int nr = static_cast<int>((a.n - r0) < kRowsPerBlock ? (a.n - r0) : kRowsPerBlock);
-        const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
-        const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
-        mbar_arrive_expect_tx(&full[s], bytes * nr);
-        uint8_t* dst = smem + s * a.stage_bytes;
-        const uint8_t* src = a.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
-        for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
+        issue(p, s);
       }
     }
   } else if (warp == W + 1) {
@@ -412,7 +513,10 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
   } else {
     // ---------------- compute ----------------
     const uint32_t xcol = a.x_off + (g < a.cols ? g : 0) * a.x_pitch;
+    const int gcol = g < a.cols ? g : 0;
     float tot[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // two independent fold chains
+    float tot2[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // ... for the second unit of a pair
+    float cm[4] = {0.f, 0.f, 0.f, 0.f};                         // bias / min terms (coef_mma)
     int64_t p = 0;
     bool ok = true;
     for (int64_t blk = 0; blk < my_blocks && ok; ++blk) {
@@ -424,19 +528,28 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
         }
         const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
         const uint32_t sbase = static_cast<uint32_t>(s * a.stage_bytes) + g * a.row_pitch;
-        for (int u = warp; u < units; u += W) {
+        auto ctx = [&](int u) {
           const int ku = (ch * a.chunk_units + u) * kUnitK;
           UnitCtx c;
           c.smem = smem;
           c.rg = sbase + u * a.unit_bytes;
           c.rg8 = c.rg + 8 * a.row_pitch;
           c.xo = xcol + 2u * ku;
-          c.xs32 = xs32t + (ku / 32) * kXsCols;
-          c.xs16 = xs16t + (ku / 16) * kXsCols;
+          c.xsh = a.xsb_off + static_cast<uint32_t>((((ku / kUnitK) * a.cols + gcol) * 4 + t) * 8);
+          c.xsl_add = a.xsb_lo;
           c.t = t;
           c.lane = lane;
-          process_unit<QT>(c, tot);
+          return c;
+        };
+        int u = warp;
+        // two units at a time, in straight-line code with separate accumulators,
+        // so the loads and MMAs of one overlap the dependency chains of the other
+        for (; u + W < units; u += 2 * W) {
+          const UnitCtx c0 = ctx(u), c1 = ctx(u + W);
+          process_unit<QT>(c0, tot, cm);
+          process_unit<QT>(c1, tot2, cm);
         }
+        if (u < units) process_unit<QT>(ctx(u), tot, cm);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
       }
@@ -445,10 +558,16 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
       const int b = static_cast<int>(blk & 1);
       if (blk >= kRedBufs && !mbar_wait(&rempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
       float* rw = red + b * (W * kRowsPerBlock * 8) + warp * (kRowsPerBlock * 8);
-      *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(tot[0] + tot[4], tot[1] + tot[5]);
-      *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(tot[2] + tot[6], tot[3] + tot[7]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) tot[i] = 0.f;
+      for (int i = 0; i < 8; ++i) tot[i] += tot2[i];
+      *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) =
+          make_float2(tot[0] + tot[4] - cm[0], tot[1] + tot[5] - cm[1]);
+      *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) =
+          make_float2(tot[2] + tot[6] - cm[2], tot[3] + tot[7] - cm[3]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tot[i] = tot2[i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cm[i] = 0.f;
       __syncwarp();
       if (lane == 0) mbar_arrive(&rfull[b]);
     }
@@ -482,12 +601,12 @@ static int unit_bytes_of(int qt) {
   }
 }
 
-// Compute warps per CTA (8 by default; GGUFMM_GEMV_WARPS=4|16 for tuning).
+// Compute warps per CTA (8 by default; GGUFMM_GEMV_WARPS=4 for tuning).
 static int compute_warps() {
   static const int w = [] {
     const char* e = std::getenv("GGUFMM_GEMV_WARPS");
     const int v = e ? std::atoi(e) : 8;
-    return v == 16 ? 16 : (v == 4 ? 4 : 8);
+    return v == 4 ? 4 : 8;
   }();
   return w;
 }
@@ -511,17 +630,16 @@ static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_bu
   a.stage_bytes = kRowsPerBlock * a.row_pitch;
   a.x_pitch = static_cast<int>(2 * k + 64);
   const int x_bytes = a.cols * a.x_pitch;
-  const int xs32_bytes = static_cast<int>(k / 32) * kXsCols * 4;
-  const int xs16_bytes = qt == kQ6_K ? static_cast<int>(k / 16) * kXsCols * 4 : 0;
+  const int xsb_half = static_cast<int>(k / kUnitK) * a.cols * 32;  // 16 bf16 slots per (unit, column)
   const int red_bytes = kRedBufs * W * kRowsPerBlock * 8 * 4;
-  const int fixed = x_bytes + xs32_bytes + xs16_bytes + red_bytes + 16 * 8 + 64;
+  const int fixed = x_bytes + 2 * xsb_half + red_bytes + 16 * 8 + 64;
   const int stages = std::min(6, (smem_budget - fixed) / a.stage_bytes);
   if (stages < 2) return false;
   a.stages = stages;
   a.x_off = static_cast<uint32_t>(stages * a.stage_bytes);
-  a.xs32_off = a.x_off + x_bytes;
-  a.xs16_off = a.xs32_off + xs32_bytes;
-  a.red_off = a.xs16_off + xs16_bytes;
+  a.xsb_off = a.x_off + x_bytes;
+  a.xsb_lo = static_cast<uint32_t>(xsb_half);
+  a.red_off = a.xsb_off + 2 * xsb_half;
   a.bar_off = (a.red_off + red_bytes + 7) / 8 * 8;
   a.nrowblocks = (n + kRowsPerBlock - 1) / kRowsPerBlock;
   return true;
@@ -549,13 +667,23 @@ static cudaError_t launch_mma_t(MmaArgs& a, int dev, const DevInfo& di, cudaStre
     }
   }
   const int64_t grid = std::min<int64_t>(a.nrowblocks, di.sms);
-  fn<<<static_cast<unsigned>(grid), (W + 2) * 32, smem, st>>>(a);
-  return cudaGetLastError();
+  // programmatic dependent launch: this kernel's weight prefetch may overlap the
+  // tail of the previous kernel on the stream (it waits before touching x / y)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3((W + 2) * 32);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 template <int QT>
 static cudaError_t launch_mma_q(MmaArgs& a, int W, int dev, const DevInfo& di, cudaStream_t st) {
-  if (W == 16) return launch_mma_t<QT, 16>(a, dev, di, st);
   if (W == 4) return launch_mma_t<QT, 4>(a, dev, di, st);
   return launch_mma_t<QT, 8>(a, dev, di, st);
 }
