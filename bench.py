@@ -6,7 +6,8 @@ Headline workload (the metric's "Q4_K GEMV"): decode
 of one Llama-3-8B-shaped layer, M=1 token, every projection Q4_K:
 q 4096->4096, k/v 4096->1024, o 4096->4096, gate/up 4096->14336,
 down 14336->4096 (218,103,808 weights = 122,683,392 bytes of GGUF blocks).
-One step = the 7 GEMV launches of one layer. ``value`` is the whole-job
+One step = the layer's 4 GEMV launches (q/k/v and gate/up each fused into one
+grouped launch, as vLLM fuses QKV and gate_up). ``value`` is the whole-job
 algorithmic HBM throughput (weight bytes + activation bytes read + output
 bytes written, per step) in GB/s, timed with CUDA events on the launching
 stream, weights resident in HBM. The weights rotate over 3 copies
@@ -44,6 +45,8 @@ LAYER = [  # (name, N = out features, K = in features) -- Llama-3-8B layer
     ("q_proj", 4096, 4096), ("k_proj", 1024, 4096), ("v_proj", 1024, 4096), ("o_proj", 4096, 4096),
     ("gate_proj", 14336, 4096), ("up_proj", 14336, 4096), ("down_proj", 4096, 14336),
 ]
+# one decode step = 4 launches: q/k/v and gate/up each fused into one grouped GEMV
+GROUPS = [("qkv", (0, 1, 2), 4096), ("o", (3,), 4096), ("gate_up", (4, 5), 4096), ("down", (6,), 14336)]
 Q4_K = 12
 QK_BYTES = 144 / 256  # bytes per Q4_K weight
 METRIC = "Q4_K GEMV HBM GB/s (% of peak); prefill dequant-GEMM TFLOP/s at 1/2/4/8 GPUs"
@@ -226,9 +229,16 @@ def run_ours(args, rank: int, world: int) -> None:
     ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _, n, _ in LAYER]
     stream = torch.cuda.current_stream(dev)
 
+    def launch(c: int, grp) -> None:
+        _, idx, k = grp
+        if len(idx) == 1:
+            ops.gemv(xs[k], layers[c][idx[0]], out=ys[idx[0]])
+        else:
+            ops.gemv_grouped(xs[k], [layers[c][i] for i in idx], outs=[ys[i] for i in idx])
+
     def step(c: int) -> None:
-        for i, (_, n, k) in enumerate(LAYER):
-            ops.gemv(xs[k], layers[c][i], out=ys[i])
+        for grp in GROUPS:
+            launch(c, grp)
 
     # warm-up (also primes attributes / driver entry points before capture)
     for i in range(max(3, args.warmup)):
@@ -265,33 +275,45 @@ def run_ours(args, rank: int, world: int) -> None:
     step_bytes = layer_bytes(m, act_bytes=2, out_bytes=4)
     value = step_bytes * steps * world / (ms / 1e3) / 1e9
 
-    # per-launch timing of the dominant kernel (every launch is gemv_kernel<Q4_K,1,1>)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(LAYER))]
-    per = [0.0] * len(LAYER)
-    nrep = 30
-    for r in range(nrep):
-        c = r % copies
-        for i, (_, n, k) in enumerate(LAYER):
-            ev[2 * i].record(stream)
-            ops.gemv(xs[k], layers[c][i], out=ys[i])
-            ev[2 * i + 1].record(stream)
+    # per-launch device time of the dominant kernel (every launch is gemv_mma_kernel<Q4_K>):
+    # each group alone in a CUDA graph of 30 launches over the rotating copies
+    per = {}
+    for grp in GROUPS:
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            for r in range(30):
+                launch(r % copies, grp)
+        gg.replay()
         torch.cuda.synchronize()
-        for i in range(len(LAYER)):
-            per[i] += ev[2 * i].elapsed_time(ev[2 * i + 1]) / nrep
-    kern_ms = sum(per)
+        e0.record(stream)
+        for _ in range(5):
+            gg.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        per[grp[0]] = e0.elapsed_time(e1) / 150
+    kern_ms = sum(per.values())
     achieved = step_bytes / (kern_ms / 1e3) / 1e9
-    # end to end through the public API: pinned host x -> device, 7 projections, y -> pinned host
-    hx = {k: torch.randn((m, k)).to(torch.bfloat16).pin_memory() for k in (4096, 14336)}
-    hy = [torch.empty((m, n), dtype=torch.float32).pin_memory() for _, n, _ in LAYER]
+
+    # end to end through the public model API (LlamaB200Model.layer_linears, the reference's
+    # per-layer projection calls): activations from pinned host memory, outputs read back
+    from vllm_webgpu_b200.models.llama import PROJ, LlamaB200Model
+    model = LlamaB200Model(None, device=dev)
+    for c in range(copies):
+        for i, (nm, _, _) in enumerate(LAYER):
+            model.weights[f"model.layers.{c}.{PROJ[nm.split('_')[0]]}"] = layers[c][i]
+    hin = {nm: torch.randn((m, kk)).to(torch.bfloat16).pin_memory()
+           for nm, kk in (("normed", 4096), ("attn_out", 4096), ("ffn_normed", 4096), ("ffn_act", 14336))}
+    bufs = {nm.split("_")[0]: torch.empty((m, n), dtype=torch.float32, device=dev) for nm, n, _ in LAYER}
+    hy = {key: torch.empty_like(b, device="cpu").pin_memory() for key, b in bufs.items()}
     e2e_steps = max(30, min(2000, steps // 10))
-    h2d = sum(m * k * 2 for _, _, k in LAYER)
-    d2h = sum(m * n * 4 for _, n, _ in LAYER)
+    h2d = sum(t.numel() * 2 for t in hin.values())
+    d2h = sum(b.numel() * 4 for b in bufs.values())
 
     def e2e_step(c: int) -> None:
-        for i, (_, n, k) in enumerate(LAYER):
-            xd = hx[k].to(dev, non_blocking=True)
-            yd = ops.mul_mat(xd, layers[c][i], out_dtype=torch.float32)
-            hy[i].copy_(yd, non_blocking=True)
+        d = {nm: t.to(dev, non_blocking=True) for nm, t in hin.items()}
+        model.layer_linears(c, d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], bufs)
+        for key, b in bufs.items():
+            hy[key].copy_(b, non_blocking=True)
         stream.synchronize()
 
     for i in range(5):
@@ -348,15 +370,15 @@ def run_ours(args, rank: int, world: int) -> None:
                        "projections": {nm: [k, n] for nm, n, k in LAYER},
                        "weight_bytes_per_step": sum(n * k // 256 * 144 for _, n, k in LAYER),
                        "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
-                       "graph": "CUDA graph of 3 steps", "parallelism": f"dp{world} (independent layer per rank)"},
+                       "graph": "CUDA graph of 3 steps", "launches_per_step": [g[0] for g in GROUPS], "parallelism": f"dp{world} (independent layer per rank)"},
             "frac_of_hbm_peak": round(value / world / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<Q4_K,M=1>", "achieved": round(achieved, 2),
+            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<Q4_K>", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": read_traffic("gemv_q4k_layer_m1"), "peak_source": peak_src,
-                         "per_launch_us": {nm: round(per[i] * 1e3, 2) for i, (nm, _, _) in enumerate(LAYER)}},
+                         "per_launch_us": {nm: round(v * 1e3, 2) for nm, v in per.items()}},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "path": "ops.mul_mat per projection, pinned host buffers"},
-            "gpu_launches": len(LAYER) * steps,
+                    "d2h_bytes_per_step": d2h, "path": "LlamaB200Model.layer_linears, pinned host buffers"},
+            "gpu_launches": len(GROUPS) * steps,
             "clocks": clocks,
             "prefill": pre,
             "cpu_baseline": cpu,
@@ -367,7 +389,7 @@ def run_ours(args, rank: int, world: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--steps", type=int, default=15000)
     ap.add_argument("--warmup", type=int, default=30)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")

@@ -114,6 +114,19 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k,
                 void* y, int y_dtype, int64_t ldy, void* stream);
 
 /*
+ * Decode GEMV of up to 4 weights that read the same activations, in one
+ * launch: y_i[m, n_i] = sum_k x[m, k] W_i[n_i, k], all W_i of one qtype and K.
+ * Replaces the separate q/k/v and gate/up dispatches of one layer
+ * (vllm_webgpu/models/llama.py:276-283 and 343-348), the way vLLM fuses
+ * QKV and gate_up projections. Same requirements and error gate as
+ * ggufmm_gemv per weight; falls back to one ggufmm_gemv per weight when the
+ * shapes cannot share a launch.
+ */
+int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                        const void* x, int x_dtype, int64_t m, int64_t ldx,
+                        void* const* y, int y_dtype, const int64_t* ldy, void* stream);
+
+/*
  * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
  * arguments). Size it once for the largest M and reuse it.
  */

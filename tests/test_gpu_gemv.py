@@ -102,3 +102,35 @@ def test_gemv_zero_and_strided_input(cuda):
 def test_gemv_no_device_timeouts(cuda):
     from vllm_webgpu_b200 import _lib
     assert _lib.lib().ggufmm_device_status(1, None) == 0
+
+
+@pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
+@pytest.mark.parametrize("m", [1, 3])
+def test_gemv_grouped_qkv_and_gate_up(cuda, qt, m):
+    """Fused q/k/v (4096, 1024, 1024 rows) and gate/up in one launch each, checked
+    per weight against the oracle."""
+    from vllm_webgpu_b200 import ops
+    k = 4096
+    for ns in ((4096, 1024, 1024), (2048, 2048)):
+        raws = [O.make_weights(n, k, qt, seed=31 + i) for i, n in enumerate(ns)]
+        ws = [_wt(r, qt, n, k) for r, n in zip(raws, ns)]
+        x = torch.from_numpy(O.make_activations(m, k, seed=7)).to(torch.bfloat16).cuda()
+        ys = ops.gemv_grouped(x, ws, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        for r, n, y in zip(raws, ns, ys):
+            assert y.shape == (m, n)
+            assert O.rel_err(y.cpu().numpy(), O.matmul_ref(x.float().cpu().numpy(), r, qt, n, k)) <= TOL
+
+
+def test_gemv_grouped_ragged_and_fallback(cuda):
+    """Segments whose N is not a multiple of 16, and 5 fp32 tokens (10 fp16 hi/lo
+    columns: more than one n8 tile, so one GEMV per weight is launched instead)."""
+    from vllm_webgpu_b200 import ops
+    for qt, k, ns, m, xd in ((O.Q4_K, 2048, (37, 5, 300), 2, torch.bfloat16), (O.Q8_0, 2048, (64, 19), 5, torch.float32)):
+        raws = [O.make_weights(n, k, qt, seed=5 + i) for i, n in enumerate(ns)]
+        ws = [_wt(r, qt, n, k) for r, n in zip(raws, ns)]
+        x = torch.from_numpy(O.make_activations(m, k, seed=9)).to(xd).cuda()
+        ys = ops.gemv_grouped(x, ws, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        for r, n, y in zip(raws, ns, ys):
+            assert O.rel_err(y.cpu().numpy(), O.matmul_ref(x.float().cpu().numpy(), r, qt, n, k)) <= TOL

@@ -21,6 +21,9 @@ cudaError_t launch_gemv(const void* q, int qtype, int64_t n, int64_t k, const vo
 cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
+cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
+                                    const int64_t* ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
                             int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
@@ -171,6 +174,31 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
                                        static_cast<cudaStream_t>(stream)));
   return cuda_status(launch_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                  static_cast<cudaStream_t>(stream)));
+}
+
+int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k, const void* x,
+                        int x_dtype, int64_t m, int64_t ldx, void* const* y, int y_dtype, const int64_t* ldy,
+                        void* stream) {
+  if (!q || !n || !y || !ldy) return GGUFMM_ERR_ARG;
+  if (nseg < 1 || nseg > 4) return GGUFMM_ERR_SHAPE;
+  for (int i = 0; i < nseg; ++i) {
+    const int s = check_matmul_args(q[i], qtype, n[i], k, x, x_dtype, m, ldx, y[i], y_dtype, ldy[i]);
+    if (s) return s;
+  }
+  if (m > 8) return GGUFMM_ERR_SHAPE;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  bool one_launch = row_bytes % 16 == 0 && aligned(x, 16) && (ldx * elem_size(x_dtype)) % 16 == 0;
+  for (int i = 0; i < nseg; ++i) one_launch = one_launch && aligned(q[i], 16) && aligned(y[i], elem_size(y_dtype));
+  int s = check_device();
+  if (s) return s;
+  if (one_launch && gemv_mma_supported(qtype, n[0], k, static_cast<int>(m), x_dtype))
+    return cuda_status(launch_gemv_mma_grouped(nseg, q, n, qtype, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
+                                               static_cast<cudaStream_t>(stream)));
+  for (int i = 0; i < nseg; ++i) {  // one GEMV per weight
+    s = ggufmm_gemv(q[i], qtype, n[i], k, x, x_dtype, m, ldx, y[i], y_dtype, ldy[i], stream);
+    if (s) return s;
+  }
+  return GGUFMM_OK;
 }
 
 static size_t round256(size_t v) { return (v + 255) / 256 * 256; }

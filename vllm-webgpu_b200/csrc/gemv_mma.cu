@@ -55,9 +55,21 @@ constexpr int kUnitK = 256;         // weights per unit (one K-quant superblock,
 constexpr int kMaxChunkUnits = 16;  // <= 4096 weights per piece
 constexpr int kRedBufs = 2;
 
-struct MmaArgs {
+// One weight of a grouped launch: several weights with the same K that read the
+// same activations (fused q/k/v, gate/up) share one launch; their row blocks are
+// numbered consecutively, segment i owning row blocks [rb0, next rb0).
+constexpr int kMaxSegs = 4;
+struct MmaSeg {
   const uint8_t* q;
+  void* y;
   int64_t n;
+  int64_t ldy;
+  int64_t rb0;
+};
+
+struct MmaArgs {
+  MmaSeg seg[kMaxSegs];
+  int nseg;
   int k;
   int64_t row_bytes;
   const void* x;
@@ -65,9 +77,7 @@ struct MmaArgs {
   int64_t ldx;
   int m;     // tokens
   int cols;  // B columns in use: m (bf16/f16 x) or 2m (fp32 x split into hi + lo fp16)
-  void* y;
   int ytype;
-  int64_t ldy;
   int unit_bytes;
   int chunk_units;
   int nchunks;
@@ -365,6 +375,14 @@ __device__ __forceinline__ void process_unit(const UnitCtx& c, float* tot, float
 }
 
 // ---- the kernel ---------------------------------------------------------------------
+__device__ __forceinline__ const MmaSeg& seg_of(const MmaArgs& a, int64_t rb) {
+  int i = 0;
+#pragma unroll
+  for (int j = 1; j < kMaxSegs; ++j)
+    if (j < a.nseg && rb >= a.seg[j].rb0) i = j;
+  return a.seg[i];
+}
+
 __device__ __forceinline__ uint32_t perm8(uint32_t e) { return (e & 4u) | ((e & 1u) << 1) | ((e >> 1) & 1u); }
 
 // W compute warps + 1 producer warp + 1 epilogue warp.
@@ -399,13 +417,14 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
   auto issue = [&](int64_t p, int s) {
     const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
     const int ch = static_cast<int>(p % a.nchunks);
-    const int64_t r0 = rb * kRowsPerBlock;
-    const int nr = static_cast<int>((a.n - r0) < kRowsPerBlock ? (a.n - r0) : kRowsPerBlock);
+    const MmaSeg& sg = seg_of(a, rb);
+    const int64_t r0 = (rb - sg.rb0) * kRowsPerBlock;
+    const int nr = static_cast<int>((sg.n - r0) < kRowsPerBlock ? (sg.n - r0) : kRowsPerBlock);
     const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
     const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
     mbar_arrive_expect_tx(&full[s], bytes * nr);
     uint8_t* dst = smem + s * a.stage_bytes;
-    const uint8_t* src = a.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
+    const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
     for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
   };
   // Weights are read-only inputs: start streaming them before anything else
@@ -496,16 +515,17 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
       if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
       const int64_t rb = blockIdx.x + blk * gridDim.x;
       const float* rbuf = red + b * (W * kRowsPerBlock * 8);
+      const MmaSeg& sg = seg_of(a, rb);
       for (int i = lane; i < kRowsPerBlock * a.m; i += 32) {
         const int row = i / a.m, tok = i - row * a.m;
-        const int64_t n_idx = rb * kRowsPerBlock + row;
+        const int64_t n_idx = (rb - sg.rb0) * kRowsPerBlock + row;
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < W; ++w) {
           v += rbuf[(w * kRowsPerBlock + row) * 8 + tok];
           if (a.cols > a.m) v += rbuf[(w * kRowsPerBlock + row) * 8 + tok + a.m];
         }
-        if (n_idx < a.n) store_y_rt(a.y, a.ytype, tok * a.ldy + n_idx, v);
+        if (n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&rempty[b]);
@@ -612,7 +632,7 @@ static int compute_warps() {
 }
 
 // Whether the tensor-core GEMV handles this problem; fills the launch plan.
-static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_budget, int W, MmaArgs& a) {
+static bool plan_mma(int qt, int64_t k, int m, int xtype, int smem_budget, int W, MmaArgs& a) {
   a.unit_bytes = unit_bytes_of(qt);
   if (!a.unit_bytes || k % kUnitK || m < 1 || m > 8) return false;
   a.cols = xtype == GGUFMM_F32 ? 2 * m : m;
@@ -641,7 +661,6 @@ static bool plan_mma(int qt, int64_t n, int64_t k, int m, int xtype, int smem_bu
   a.xsb_lo = static_cast<uint32_t>(xsb_half);
   a.red_off = a.xsb_off + 2 * xsb_half;
   a.bar_off = (a.red_off + red_bytes + 7) / 8 * 8;
-  a.nrowblocks = (n + kRowsPerBlock - 1) / kRowsPerBlock;
   return true;
 }
 
@@ -650,7 +669,8 @@ bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const DevInfo di = device_info(dev);
-  return plan_mma(qtype, n, k, m, xtype, std::min(di.smem_optin, 227 * 1024), compute_warps(), a);
+  (void)n;
+  return plan_mma(qtype, k, m, xtype, std::min(di.smem_optin, 227 * 1024), compute_warps(), a);
 }
 
 template <int QT, int W>
@@ -688,27 +708,38 @@ static cudaError_t launch_mma_q(MmaArgs& a, int W, int dev, const DevInfo& di, c
   return launch_mma_t<QT, 8>(a, dev, di, st);
 }
 
-cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
-                            int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st) {
+// nseg weights of the same qtype and K (each 16-byte aligned, row bytes a
+// multiple of 16) against the same activations, one launch.
+cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
+                                    const int64_t* ldy, int64_t row_bytes, cudaStream_t st) {
+  if (nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const DevInfo di = device_info(dev);
   const int W = compute_warps();
   MmaArgs a{};
-  if (!plan_mma(qtype, n, k, static_cast<int>(m), xtype, std::min(di.smem_optin, 227 * 1024), W, a))
+  if (!plan_mma(qtype, k, static_cast<int>(m), xtype, std::min(di.smem_optin, 227 * 1024), W, a))
     return cudaErrorInvalidValue;
-  a.q = static_cast<const uint8_t*>(q);
-  a.n = n;
+  a.nseg = nseg;
+  int64_t rb = 0;
+  for (int i = 0; i < nseg; ++i) {
+    a.seg[i].q = static_cast<const uint8_t*>(q[i]);
+    a.seg[i].y = y[i];
+    a.seg[i].n = n[i];
+    a.seg[i].ldy = ldy[i];
+    a.seg[i].rb0 = rb;
+    rb += (n[i] + kRowsPerBlock - 1) / kRowsPerBlock;
+  }
+  a.nrowblocks = rb;
   a.k = static_cast<int>(k);
   a.row_bytes = row_bytes;
   a.x = x;
   a.xtype = xtype;
   a.ldx = ldx;
   a.m = static_cast<int>(m);
-  a.y = y;
   a.ytype = ytype;
-  a.ldy = ldy;
   switch (qtype) {
     case kQ4_K: return launch_mma_q<kQ4_K>(a, W, dev, di, st);
     case kQ4_0: return launch_mma_q<kQ4_0>(a, W, dev, di, st);
@@ -716,6 +747,11 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
     case kQ6_K: return launch_mma_q<kQ6_K>(a, W, dev, di, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
+                            int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st) {
+  return launch_gemv_mma_grouped(1, &q, &n, qtype, k, x, xtype, m, ldx, &y, ytype, &ldy, row_bytes, st);
 }
 
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }

@@ -1,7 +1,9 @@
 """The Llama layer's quantized projections, called the way the reference's
 ``LlamaWebGPUModel._transformer_layer`` calls them
 (vllm_webgpu/models/llama.py:276-283 q/k/v, :328-332 o, :343-348 gate/up,
-:355-359 down), each through ``_dispatch("matmul_quant", ...)``.
+:355-359 down), each through ``_dispatch("matmul_quant", ...)``. In decode
+(M <= 8) the projections that share an input -- q/k/v and gate/up -- run as
+one grouped launch (ggufmm_gemv_grouped), as vLLM fuses QKV and gate_up.
 
 The reference picks ``USE_QUANT = 0 if q_proj.weight is present`` and so never
 runs its quantized branch (llama.py:258); here the branch is chosen by the
@@ -12,6 +14,7 @@ from __future__ import annotations
 
 import torch
 
+from .. import ops
 from ..formats import GGUFQuantTensor
 from .base import BaseB200Model
 
@@ -35,17 +38,31 @@ class LlamaB200Model(BaseB200Model):
                        ((n + 255) // 256, 1, 1))
         return out
 
+    def _fused(self, x: torch.Tensor, ws: list, bufs: list) -> bool:
+        """One grouped launch for projections that read the same input (decode,
+        M <= 8, all GGUF-quantized with one qtype); False if not applicable."""
+        if (x.reshape(-1, x.shape[-1]).shape[0] > ops.GEMV_MAX_M or
+                not all(isinstance(w, GGUFQuantTensor) for w in ws) or len({w.qtype for w in ws}) != 1
+                or len({b.dtype for b in bufs}) != 1):
+            return False
+        ops.gemv_grouped(x, ws, outs=[b.reshape(-1, w.n) for b, w in zip(bufs, ws)])
+        return True
+
     def project_qkv(self, layer: int, normed: torch.Tensor, q_buf, k_buf, v_buf):
-        for buf, p in ((q_buf, "q"), (k_buf, "k"), (v_buf, "v")):
-            self._linear(normed, self._w(layer, p), buf)
+        ws = [self._w(layer, p) for p in ("q", "k", "v")]
+        if not self._fused(normed, ws, [q_buf, k_buf, v_buf]):
+            for buf, w in zip((q_buf, k_buf, v_buf), ws):
+                self._linear(normed, w, buf)
         return q_buf, k_buf, v_buf
 
     def project_o(self, layer: int, attn_out: torch.Tensor, out: torch.Tensor):
         return self._linear(attn_out, self._w(layer, "o"), out)
 
     def project_gate_up(self, layer: int, ffn_normed: torch.Tensor, gate_buf, up_buf):
-        self._linear(ffn_normed, self._w(layer, "gate"), gate_buf)
-        self._linear(ffn_normed, self._w(layer, "up"), up_buf)
+        ws = [self._w(layer, "gate"), self._w(layer, "up")]
+        if not self._fused(ffn_normed, ws, [gate_buf, up_buf]):
+            self._linear(ffn_normed, ws[0], gate_buf)
+            self._linear(ffn_normed, ws[1], up_buf)
         return gate_buf, up_buf
 
     def project_down(self, layer: int, ffn_act: torch.Tensor, out: torch.Tensor):

@@ -89,6 +89,35 @@ def gemv(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
     return y
 
 
+def gemv_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Tensor] | None = None,
+                 out_dtype: torch.dtype | None = None) -> list[torch.Tensor]:
+    """Decode GEMV of up to 4 weights sharing the activations (fused q/k/v or
+    gate/up) in one launch; returns one [M, N_i] output per weight."""
+    if not 1 <= len(ws) <= 4:
+        raise ValueError("gemv_grouped takes 1 to 4 weights")
+    k, qt = ws[0].k, ws[0].qtype
+    if any(w.k != k or w.qtype != qt for w in ws):
+        raise ValueError("grouped weights must share K and the quantization type")
+    dev = _require_cuda(x, *[w.data for w in ws])
+    x2 = _as_2d(x, k)
+    if outs is None:
+        outs = [None] * len(ws)
+    ys = [_out(x2, w.n, o, out_dtype) for w, o in zip(ws, outs)]
+    if len({y.dtype for y in ys}) != 1:
+        raise ValueError("grouped outputs must share a dtype")
+    import ctypes
+    nseg = len(ws)
+    qs = (ctypes.c_void_p * nseg)(*[w.data.data_ptr() for w in ws])
+    ns = (ctypes.c_int64 * nseg)(*[w.n for w in ws])
+    yp = (ctypes.c_void_p * nseg)(*[y.data_ptr() for y in ys])
+    ld = (ctypes.c_int64 * nseg)(*[y.stride(0) for y in ys])
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemv_grouped(nseg, qs, ns, qt, k, x2.data_ptr(), _code(x2.dtype), x2.shape[0],
+                                            x2.stride(0), yp, _code(ys[0].dtype), ld, _stream(dev))
+    _lib.check(st, "ggufmm_gemv_grouped")
+    return ys
+
+
 _workspaces: dict[int, torch.Tensor] = {}
 
 
