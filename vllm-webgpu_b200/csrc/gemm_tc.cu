@@ -105,7 +105,9 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kTileW, m0 = blockIdx.y * BN;
+  // token tiles vary fastest: the CTAs that share one weight tile run together,
+  // so the weight (the large operand) streams from HBM once and the rest hit L2
+  const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTileW;
   const int nk = (k + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -245,7 +247,7 @@ static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, i
       g_gemm_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
     }
   }
-  dim3 grid(static_cast<unsigned>((n + kTileW - 1) / kTileW), static_cast<unsigned>((m + BN - 1) / BN));
+  dim3 grid(static_cast<unsigned>((m + BN - 1) / BN), static_cast<unsigned>((n + kTileW - 1) / kTileW));
   fn<<<grid, 192, L::kTotal, st>>>(mw, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
                                    static_cast<int>(k));
   return cudaGetLastError();
