@@ -12,15 +12,38 @@
 
 namespace ggufmm {
 
-// Load `NW` 32-bit words starting at a 2-byte-aligned global address.
+// Load `NW` 32-bit words starting at a 2-byte-aligned global address: aligned
+// 32-bit loads (16-byte vector loads when the address allows) and a funnel shift.
+// Only words that hold requested bytes are touched.
 template <int NW>
 __device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* w) {
-  const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (NW % 4 == 0 && (a & 15) == 0) {
+    const uint4* v = reinterpret_cast<const uint4*>(p);
 #pragma unroll
-  for (int i = 0; i < NW; ++i) {
-    uint32_t lo = __ldg(h + 2 * i), hi = __ldg(h + 2 * i + 1);
-    w[i] = lo | (hi << 16);
+    for (int i = 0; i < NW / 4; ++i) {
+      const uint4 t = __ldg(v + i);
+      w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+    }
+    return;
   }
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+  if ((a & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = __ldg(q + i);
+    return;
+  }
+  uint32_t t[NW + 1];
+#pragma unroll
+  for (int i = 0; i <= NW; ++i) t[i] = __ldg(q + i);
+#pragma unroll
+  for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(t[i], t[i + 1], 16);
+}
+
+// Exact float of a small integer (|v| < 2^22) without the quarter-rate int->float
+// conversion: 1.5*2^23 + v has v in its low mantissa bits; one add removes the offset.
+__device__ __forceinline__ float small_int_to_float(int v) {
+  return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.f);
 }
 
 __device__ __forceinline__ uint32_t byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xFFu; }
@@ -38,8 +61,8 @@ __device__ __forceinline__ void dequant32<kQ4_0>(const uint8_t* row, int unit, f
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     uint32_t v = byte_of(w, j);
-    o[j] = __fmul_rn(d, static_cast<float>(static_cast<int>(v & 15u) - 8));
-    o[j + 16] = __fmul_rn(d, static_cast<float>(static_cast<int>(v >> 4) - 8));
+    o[j] = __fmul_rn(d, small_int_to_float(static_cast<int>(v & 15u) - 8));
+    o[j + 16] = __fmul_rn(d, small_int_to_float(static_cast<int>(v >> 4) - 8));
   }
 }
 
@@ -53,7 +76,7 @@ __device__ __forceinline__ void dequant32<kQ8_0>(const uint8_t* row, int unit, f
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     int q = static_cast<int>(static_cast<int8_t>(byte_of(w, j)));
-    o[j] = __fmul_rn(static_cast<float>(q), d);
+    o[j] = __fmul_rn(small_int_to_float(q), d);
   }
 }
 
@@ -87,7 +110,7 @@ __device__ __forceinline__ void dequant32<kQ4_K>(const uint8_t* row, int unit, f
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     uint32_t q = (byte_of(w, i) >> sh) & 15u;
-    o[i] = __fsub_rn(__fmul_rn(dsc, static_cast<float>(q)), dm);
+    o[i] = __fsub_rn(__fmul_rn(dsc, small_int_to_float(static_cast<int>(q))), dm);
   }
 }
 
@@ -109,36 +132,53 @@ __device__ __forceinline__ void dequant32<kQ6_K>(const uint8_t* row, int unit, f
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
     int q = static_cast<int>(((byte_of(ql, c) >> shl) & 15u) | (((byte_of(qh, c) >> shh) & 3u) << 4)) - 32;
-    o[c] = __fmul_rn(c < 16 ? dl0 : dl1, static_cast<float>(q));
+    o[c] = __fmul_rn(c < 16 ? dl0 : dl1, small_int_to_float(q));
   }
 }
 
+// The 32 outputs of a lane are staged in shared memory (XOR-swizzled 16-byte
+// slots, conflict-free) so that every global store instruction of a warp writes
+// 512 contiguous bytes.
 template <int QT, int OT>
 __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ q, int64_t n_units,
                                                       int units_per_row, int64_t row_bytes,
                                                       void* __restrict__ out) {
+  constexpr int kChunks = OT == GGUFMM_F32 ? 8 : 4;  // 16-byte chunks per lane (32 outputs)
+  __shared__ uint4 stage[8][32 * kChunks];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (u >= n_units) return;
-  const int64_t r = u / units_per_row;
-  const int c = static_cast<int>(u - r * units_per_row);
-  float v[32];
-  dequant32<QT>(q + r * row_bytes, c, v);
-  if (OT == GGUFMM_F32) {
-    float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + u * 32);
+  const int64_t warp_u0 = u - lane;
+  uint4* st = stage[wid];
+  if (u < n_units) {
+    const int64_t r = u / units_per_row;
+    const int c = static_cast<int>(u - r * units_per_row);
+    float v[32];
+    dequant32<QT>(q + r * row_bytes, c, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  } else {
-    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(out) + u * 32);
+    for (int i = 0; i < kChunks; ++i) {
+      uint4 w;
+      if (OT == GGUFMM_F32) {
+        w = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
+                       __float_as_uint(v[4 * i + 3]));
+      } else {
+        uint32_t h[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      uint32_t w[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        __half2 h2 = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
-        w[j] = *reinterpret_cast<uint32_t*>(&h2);
+        for (int j = 0; j < 4; ++j) {
+          __half2 h2 = __floats2half2_rn(v[8 * i + 2 * j], v[8 * i + 2 * j + 1]);
+          h[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        w = make_uint4(h[0], h[1], h[2], h[3]);
       }
-      o[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      st[lane * kChunks + (i ^ (lane & (kChunks - 1)))] = w;
     }
+  }
+  __syncwarp();
+  uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out)) + warp_u0 * kChunks;
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const int gi = j * 32 + lane;  // 16-byte chunk index within the warp's output range
+    const int src = gi / kChunks, ch = gi % kChunks;
+    if (warp_u0 + src < n_units) o[gi] = st[src * kChunks + (ch ^ (src & (kChunks - 1)))];
   }
 }
 
