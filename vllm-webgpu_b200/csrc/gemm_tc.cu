@@ -20,7 +20,7 @@
 //   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM (each warp owns the 32
 //               TMEM lanes its warp-in-quad index selects), transpose on the
 //               fly, coalesced stores of Y.
-// No TMA multicast is used anywhere (safe on multi-GPU jobs).
+// Every TMA load is a plain (single-CTA) load of this GPU's own memory.
 #include <algorithm>
 #include <mutex>
 #include <set>
