@@ -6,6 +6,7 @@
 // vllm_webgpu/models/llama.py:45-54; FileNotFoundError/RuntimeError for a
 // missing pipeline in vllm_webgpu/webgpu/pipeline.py:25-30).
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -19,6 +20,9 @@ cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, 
 cudaError_t launch_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
                         int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
+                                  int64_t ldy, cudaStream_t st);
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
 cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -136,12 +140,13 @@ const char* ggufmm_status_string(int s) {
 
 int ggufmm_device_status(int clear, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int a = 0, b = 0, c = 0;
+  int a = 0, b = 0, c = 0, d = 0;
   cudaError_t e = gemv_device_error(&a, clear, st);
   if (e == cudaSuccess) e = gemm_device_error(&b, clear, st);
   if (e == cudaSuccess) e = gemv_mma_device_error(&c, clear, st);
+  if (e == cudaSuccess) e = gemm_fused_device_error(&d, clear, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return a | b | c;
+  return a | b | c | d;
 }
 
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
@@ -203,6 +208,15 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
 
 static size_t round256(size_t v) { return (v + 255) / 256 * 256; }
 
+// GGUFMM_GEMM_FUSED=0 selects the two-pass (dequantize, then GEMM) path for Q4_K too.
+static bool fused_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GGUFMM_GEMM_FUSED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 size_t ggufmm_gemm_workspace_size(int qtype, int64_t m, int64_t n, int64_t k) {
   if (!block_of(qtype) || m <= 0 || n <= 0 || k <= 0 || k % block_of(qtype)) return 0;
   return round256(static_cast<size_t>(n) * k * 2) + round256(static_cast<size_t>(m) * k * 2);
@@ -220,6 +234,14 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   s = check_device();
   if (s) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (qtype == kQ4_K && m <= 128 && aligned(q, 16) && fused_gemm_enabled()) {
+    // dequantization fused into the tensor-core GEMM (one token tile: every weight is
+    // decoded once): only the fp16 activations need scratch. Above one token tile the
+    // two-pass path dequantizes each weight once instead of once per token tile.
+    cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, workspace, st);
+    if (e == cudaSuccess) e = launch_gemm_fused_q4k(q, workspace, n, m, k, y, y_dtype, ldy, st);
+    return cuda_status(e);
+  }
   uint8_t* w16 = static_cast<uint8_t*>(workspace);
   uint8_t* x16 = w16 + round256(static_cast<size_t>(n) * k * 2);
   cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);

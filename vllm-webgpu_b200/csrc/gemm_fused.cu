@@ -1,0 +1,273 @@
+// gemm_fused.cu -- Q4_K GEMM on the sm_100a tensor cores with the dequantization
+// fused into the pipeline: Y[m, n] = sum_k X[m, k] W[n, k] for any M.
+//
+// The two-pass GEMM (dequantize the whole weight to fp16 in scratch, then a
+// tcgen05 GEMM) moves 4.5 bytes per weight through HBM (0.56 read, 2 written,
+// 2 read again). Here each CTA streams the packed GGUF bytes of its 128 weight
+// rows once (0.56 B per weight) and turns them into fp16 MMA operands in shared
+// memory, next to the tensor cores.
+//
+// CTA = 14 warps, one 128 (weight rows, MMA M) x BN (tokens, MMA N) tile:
+//   warp 0       TMA producer: per 128-weight k-block, the rows' 16-byte Q4_K
+//                headers (d, dmin, 6-bit scales) and 64 bytes of nibbles (2-D
+//                uint8 tensor maps, no swizzle), and the activation tile (fp16,
+//                128-byte swizzle); one mbarrier transaction count per stage.
+//   warps 6..13  dequantizers: thread (row r, half q) decodes the 64 weights of
+//                one nibble chunk to fp32 exactly as gguf-py does
+//                ((d*sc)*q - dmin*m; the product is exact, so one fma), rounds
+//                once to fp16 and writes them in the 128-byte-swizzled K-major
+//                layout tcgen05.mma reads; fence.proxy.async makes the generic
+//                stores visible to the tensor core before the warp arrives.
+//   warp 1       allocates TMEM and issues tcgen05.mma (kind::f16, M=128,
+//                N=BN, K=16) from one elected lane; each stage is committed back
+//                to the producer, the last one to the epilogue.
+//   warps 2..5   epilogue: tcgen05.ld of the fp32 accumulator, transposed
+//                stores of Y.
+// Operand precision is that of the two-pass GEMM: the exact fp32 dequantized
+// weight rounded once to fp16, activations in fp16, fp32 accumulation.
+#include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "tcgen05.cuh"
+
+namespace ggufmm {
+
+constexpr int kFKB = 128;      // weights per k-block (half a Q4_K superblock)
+constexpr int kDqWarps = 8;
+constexpr int kFusedThreads = (6 + kDqWarps) * 32;
+
+template <int BN>
+struct FusedSmem {
+  static constexpr uint32_t kA = kTileW * kFKB * 2;  // 2 swizzle atoms of 128 rows x 64 fp16
+  static constexpr uint32_t kB = BN * kFKB * 2;      // 2 atoms of BN rows
+  static constexpr uint32_t kHdr = kTileW * 16;
+  static constexpr uint32_t kQs = kTileW * 64;
+  static constexpr uint32_t kStage = kA + kB + kHdr + kQs;
+  static constexpr int kStages = (224 * 1024) / kStage < 4 ? (224 * 1024) / kStage : 4;
+  static constexpr uint32_t kBarOff = kStages * kStage;
+  static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Exact float of a small non-negative integer (< 2^22).
+__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
+  return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    gemm_fused_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
+                          const __grid_constant__ CUtensorMap tm_x, void* __restrict__ y, int ytype, int64_t ldy,
+                          int n, int m, int k) {
+  using L = FusedSmem<BN>;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* afull = full + S;
+  uint64_t* empty = afull + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTileW;
+  const int nkb = k / kFKB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&afull[s], kDqWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN < 32 ? 32 : BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S;
+        if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1)) break;
+        uint8_t* st = smem + s * L::kStage;
+        const int sb = kb >> 1, h = kb & 1;
+        mbar_arrive_expect_tx(&full[s], L::kB + L::kHdr + L::kQs);
+        tma_load_2d(st + L::kA + L::kB, &tm_hdr, 144 * sb, n0, &full[s]);
+        tma_load_2d(st + L::kA + L::kB + L::kHdr, &tm_qs, 144 * sb + 16 + 64 * h, n0, &full[s]);
+        tma_load_2d(st + L::kA, &tm_x, kb * kFKB, m0, &full[s]);
+        tma_load_2d(st + L::kA + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16<BN>();
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % S;
+        const uint32_t par = (kb / S) & 1;
+        if (!mbar_wait(&full[s], par) || !mbar_wait(&afull[s], par)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
+        const uint32_t b_addr = a_addr + L::kA;
+#pragma unroll
+        for (int atom = 0; atom < 2; ++atom) {
+          const uint64_t adesc = umma_smem_desc(a_addr + atom * (kTileW * 128));
+          const uint64_t bdesc = umma_smem_desc(b_addr + atom * (BN * 128));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem_d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || atom > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  } else if (warp < 6) {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;
+    const bool ok = mbar_wait(accum, 0);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const int nrow = n0 + quad * 32 + lane;
+      const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c0, r);
+        if (nrow < n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int mm = m0 + c0 + j;
+            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- dequantizers ----------------
+    const int dt = (warp - 6) * 32 + lane;
+    const int r = dt & (kTileW - 1), q = dt >> 7;  // row, 64-weight half of the k-block
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % S;
+      if (!mbar_wait(&full[s], (kb / S) & 1)) break;
+      uint8_t* st = smem + s * L::kStage;
+      const uint4 hd = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + r * 16);
+      const uint4 q0 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32 + 16);
+      // nibble chunk c of the superblock: low nibbles = sub-block 2c, high = 2c+1
+      const int c = 2 * (kb & 1) + q;
+      const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
+      // 6-bit scales/mins (gguf quants.py:479-501), branch-free over c
+      const uint32_t hi_sel = 0u - static_cast<uint32_t>(c >> 1);
+      const uint32_t scw = ((hd.y & 0x3F3F3F3Fu) & ~hi_sel) | (((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) & hi_sel);
+      const uint32_t mw = ((hd.z & 0x3F3F3F3Fu) & ~hi_sel) | ((((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u)) & hi_sel);
+      const uint32_t sh = 16u * (c & 1);
+      const float dsc_lo = __fmul_rn(d, small_uint_to_float((scw >> sh) & 0xFFu));
+      const float dsc_hi = __fmul_rn(d, small_uint_to_float((scw >> (sh + 8)) & 0xFFu));
+      const float ndm_lo = -__fmul_rn(dmin, small_uint_to_float((mw >> sh) & 0xFFu));
+      const float ndm_hi = -__fmul_rn(dmin, small_uint_to_float((mw >> (sh + 8)) & 0xFFu));
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      uint8_t* arow = st + q * (kTileW * 128) + r * 128;  // atom q, row r
+#pragma unroll
+      for (int kc = 0; kc < 8; ++kc) {  // 16-byte output chunk: 8 consecutive k of the atom
+        // k 0..31 = low nibbles of bytes 0..31, k 32..63 = high nibbles
+        const bool hi = kc >= 4;
+        const uint32_t wa = w[(kc & 3) * 2], wb = w[(kc & 3) * 2 + 1];
+        const int shn = hi ? 4 : 0;
+        const float ds = hi ? dsc_hi : dsc_lo, nd = hi ? ndm_hi : ndm_lo;
+        uint32_t out[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t src = e < 2 ? wa : wb;
+          const int b0 = (2 * e) & 3;
+          const float v0 = fmaf(ds, small_uint_to_float((src >> (8 * b0 + shn)) & 15u), nd);
+          const float v1 = fmaf(ds, small_uint_to_float((src >> (8 * (b0 + 1) + shn)) & 15u), nd);
+          __half2 h2 = __floats2half2_rn(v0, v1);
+          out[e] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(arow + ((kc ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to tcgen05.mma
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(BN < 32 ? 32 : BN)
+                 : "memory");
+  }
+}
+
+// ---- host side --------------------------------------------------------------
+// uint8 2-D map over the GGUF bytes [rows, row_bytes], box = box_bytes x 128 rows.
+static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes), static_cast<cuuint32_t>(kTileW)};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static std::mutex g_fused_attr_mu;
+static std::set<std::pair<const void*, int>> g_fused_attr_done;
+
+template <int BN>
+static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
+                                   int ytype, int64_t ldy, cudaStream_t st) {
+  using L = FusedSmem<BN>;
+  const int64_t row_bytes = k / 256 * 144;
+  CUtensorMap mh, mq, mx;
+  if (!make_map_q(&mh, q, n, row_bytes, 16) || !make_map_q(&mq, q, n, row_bytes, 64) ||
+      !make_map_f16(&mx, x16, m, k, BN))
+    return cudaErrorInvalidValue;
+  auto fn = gemm_fused_q4k_kernel<BN>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(g_fused_attr_mu);
+    if (!g_fused_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::kTotal));
+      if (e != cudaSuccess) return e;
+      g_fused_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
+    }
+  }
+  dim3 grid(static_cast<unsigned>((m + BN - 1) / BN), static_cast<unsigned>((n + kTileW - 1) / kTileW));
+  fn<<<grid, kFusedThreads, L::kTotal, st>>>(mh, mq, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
+                                              static_cast<int>(k));
+  return cudaGetLastError();
+}
+
+// Q4_K weights q (16-byte aligned GGUF blocks [n, k/256*144]) times fp16 activations
+// x16 [m, k] (row-major, 16-byte aligned).
+cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
+                                  int64_t ldy, cudaStream_t st) {
+  if (m <= 32) return launch_fused_bn<32>(q, x16, n, m, k, y, ytype, ldy, st);
+  if (m <= 64) return launch_fused_bn<64>(q, x16, n, m, k, y, ytype, ldy, st);
+  return launch_fused_bn<128>(q, x16, n, m, k, y, ytype, ldy, st);
+}
+
+cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+
+}  // namespace ggufmm
