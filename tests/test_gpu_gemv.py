@@ -45,9 +45,12 @@ def test_gemv_layer_shapes_m1(cuda, qt, n, k):
 
 @pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
 @pytest.mark.parametrize("n,k,m", [(1, 2048, 1), (5, 2048, 3), (7, 6144, 2), (13, 18432, 1), (9, 32768, 1),
-                                   (3, 65536, 1)])
+                                   (3, 65536, 1), (18, 1024, 2), (33, 8192, 1), (40, 12288, 1), (21, 256, 8)])
 def test_gemv_ragged_and_wide(cuda, qt, n, k, m):
-    """N not a multiple of the row tile; K needing 1, 2 or more segments per thread."""
+    """N not a multiple of the row tile (row groups copied whole, partly filled);
+    K in one piece, in several pieces, and with a short last piece."""
+    if qt == O.Q6_K and (k // 256 * 210) % 16:
+        pytest.skip("Q6_K rows of this K are not a multiple of 16 bytes (rejected with ERR_ALIGN)")
     y, ref = _run(qt, m, n, k)
     assert O.rel_err(y, ref) <= TOL
 

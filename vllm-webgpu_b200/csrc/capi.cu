@@ -31,6 +31,11 @@ cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_
 cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, const void* x, int xtype, int64_t m,
                             int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st);
+bool gemv_i8_supported(int qtype, int64_t k, int m);
+cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                                   const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                             int64_t ldy, cudaStream_t st);
 
@@ -140,13 +145,14 @@ const char* ggufmm_status_string(int s) {
 
 int ggufmm_device_status(int clear, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int a = 0, b = 0, c = 0, d = 0;
+  int a = 0, b = 0, c = 0, d = 0, f = 0;
   cudaError_t e = gemv_device_error(&a, clear, st);
   if (e == cudaSuccess) e = gemm_device_error(&b, clear, st);
   if (e == cudaSuccess) e = gemv_mma_device_error(&c, clear, st);
   if (e == cudaSuccess) e = gemm_fused_device_error(&d, clear, st);
+  if (e == cudaSuccess) e = gemv_i8_device_error(&f, clear, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return a | b | c | d;
+  return a | b | c | d | f;
 }
 
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
@@ -172,8 +178,12 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   if (row_bytes > 160 * 1024) return GGUFMM_ERR_SHAPE;  // one weight row must fit a shared-memory stage
   s = check_device();
   if (s) return s;
-  // tensor-core GEMV when the shape allows (K a multiple of 256, activations fit
-  // in shared memory), else the CUDA-core streaming GEMV
+  // integer tensor-core GEMV (Q4_K, Q4_0), else the fp16 tensor-core GEMV when the
+  // shape allows (K a multiple of 256, activations fit in shared memory), else the
+  // CUDA-core streaming GEMV
+  if (gemv_i8_supported(qtype, k, static_cast<int>(m)))
+    return cuda_status(launch_gemv_i8_grouped(1, &q, &n, qtype, k, x, x_dtype, m, ldx, &y, y_dtype, &ldy, row_bytes,
+                                              static_cast<cudaStream_t>(stream)));
   if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype))
     return cuda_status(launch_gemv_mma(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                        static_cast<cudaStream_t>(stream)));
@@ -196,6 +206,9 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
   for (int i = 0; i < nseg; ++i) one_launch = one_launch && aligned(q[i], 16) && aligned(y[i], elem_size(y_dtype));
   int s = check_device();
   if (s) return s;
+  if (one_launch && gemv_i8_supported(qtype, k, static_cast<int>(m)))
+    return cuda_status(launch_gemv_i8_grouped(nseg, q, n, qtype, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
+                                              static_cast<cudaStream_t>(stream)));
   if (one_launch && gemv_mma_supported(qtype, n[0], k, static_cast<int>(m), x_dtype))
     return cuda_status(launch_gemv_mma_grouped(nseg, q, n, qtype, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                                static_cast<cudaStream_t>(stream)));

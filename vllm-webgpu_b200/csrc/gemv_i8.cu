@@ -1,0 +1,752 @@
+// gemv_i8.cu -- decode GEMV (M <= 8 tokens) for Q4_K and Q4_0 on the integer
+// tensor-core path (mma.sync m16n8k32, u8 weights x s8 activation digits,
+// s32 accumulation), straight from GGUF blocks.
+//
+//   y[m, n] = sum_k x[m, k] W[n, k]
+//
+// Why integers: at HBM speed the cost of a 4-bit GEMV is the per-weight decode,
+// and on the u8 path a 4-bit quant is ready for the MMA after ONE lop3 per FOUR
+// weights (w & 0x0F0F0F0F are four u8 quants; Q4_K high nibbles are used in
+// place, w & 0xF0F0F0F0 = 16 q). One m16n8k32 consumes 512 weights.
+//
+// Activations as exact integer digits: every 256 consecutive activations of a
+// token (one K-quant superblock, 8 Q4_0 blocks) get a power-of-two scale s with
+// max|x| / s in [2^21, 2^22), and X = rint(x / s) is written as three balanced
+// signed bytes, X = 65536 d1 + 256 d2 + d3. Each digit is one B column of the
+// MMA (the n8 tile holds the 3 digits of up to 2 tokens for free), so the MMA
+// result is exact and the only rounding of x is rint at 2^-22 of the group
+// maximum (fp32-like; bf16 / fp16 inputs are mostly exact).
+//
+// Scales, exactly:
+//   Q4_K  value = d sc_j q - dmin m_j (j = 32-weight sub-block). Per unit the
+//         integer sum T = sum_j sc_j * acc_j is formed with integer multiply-adds
+//         (acc_j = one MMA, highs carry the factor 16 and lows get it at the
+//         end), converted once and folded with (d / 16) * s * radix. The min
+//         part dmin * sum_j m_j X_j runs as a bf16 MMA with the exact 6-bit m_j
+//         against the per-sub-block sums of x (bf16 hi + lo).
+//   Q4_0  value = d (q - 8): the MMA's C operand carries -8 * sum(digits of the
+//         block), so each block's accumulator is sum (q - 8) X exactly; folded
+//         with the block's fp16 d.
+// Precision is therefore that of fp32 arithmetic on the exact dequantized
+// weights (the reference's dequantize-then-matmul), not an fp16 weight.
+//
+// Pipeline: one producer warp streams pieces (16 rows x up to 32 units of 256
+// weights) into a shared-memory ring with 1-D bulk copies of >= 4 KB where the
+// layout allows (several whole rows per copy: short copies are request-bound);
+// W compute warps take every W-th unit; one epilogue warp sums the warps'
+// partials of a row block and writes y. The producer takes no part in staging
+// x, so its copy back-pressure never stalls the other warps. Bounded mbarrier
+// waits throughout.
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+
+namespace ggufmm {
+
+namespace {
+
+constexpr int kRows = 16;
+constexpr int kUnitK = 256;
+constexpr int kCopyBytes = 4608;  // target bytes per bulk copy
+constexpr int kRedBufs = 2;
+constexpr int kMaxSegs = 4;
+constexpr int kW = 8;  // compute warps
+constexpr int kThreads = (kW + 2) * 32;
+
+struct Seg {
+  const uint8_t* q;
+  void* y;
+  int64_t n;
+  int64_t ldy;
+  int64_t rb0;
+};
+
+struct I8Args {
+  Seg seg[kMaxSegs];
+  int nseg;
+  int k;
+  int64_t row_bytes;
+  const void* x;
+  int xtype;
+  int64_t ldx;
+  int m;
+  int ytype;
+  int unit_bytes;
+  int chunk_units;
+  int nchunks;
+  int chunk_bytes;
+  int rg;            // rows per bulk copy (several whole rows when one chunk spans the row)
+  int group_pitch;   // smem bytes per copied row group (32 mod 128)
+  int stage_bytes;
+  int stages;
+  int64_t nrowblocks;
+  int xd_pitch;      // bytes per digit column of x
+  int red_stride;    // floats per warp in one reduction buffer
+  uint32_t xd_off;   // int8 digits [3m cols][k]
+  uint32_t xf_off;   // float fold factors [unit][8 NCG cols]: s * radix
+  uint32_t xs_off;   // Q4_K: bf16 x sums [unit][8 NCC cols][8 sub-blocks]; Q4_0: int -8*digit sums [block][8 NCG cols]
+  uint32_t red_off;
+  uint32_t bar_off;
+};
+
+__device__ __forceinline__ void imma(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                     uint32_t b1, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+
+__device__ __forceinline__ void mma_bf16_z(float* d, uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(0u), "r"(0u), "r"(b0), "r"(0u), "f"(0.f));
+}
+
+template <typename T>
+__device__ __forceinline__ T lds(const uint8_t* smem, uint32_t off) {
+  return *reinterpret_cast<const T*>(smem + off);
+}
+
+// 4 bytes at a 2-byte aligned offset.
+__device__ __forceinline__ uint32_t lds32_a2(const uint8_t* smem, uint32_t off) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(smem + (off & ~3u));
+  return __funnelshift_r(w[0], w[1], (off & 3u) * 8u);
+}
+
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return __byte_perm(w, 0u, 0x4440u | i); }
+
+// bf16 bits of a small non-negative integer (exact), packed as (lo, hi).
+__device__ __forceinline__ uint32_t bf16x2_of_small(uint32_t lo, uint32_t hi) {
+  const uint32_t fl = __float_as_uint(static_cast<float>(lo)), fh = __float_as_uint(static_cast<float>(hi));
+  return __byte_perm(fl, fh, 0x7632u);
+}
+
+struct Ctx {
+  const uint8_t* smem;
+  uint32_t rg, rg8;  // unit's bytes in the weight rows of MMA rows g, g+8
+  uint32_t xo[3];    // digit column (per col group) + unit's first k + 8t
+  uint32_t xf;       // fold factors of this unit, cols 2t, 2t+1 of col group 0
+  uint32_t xs;       // Q4_K: x-sum word (unit, coef col g, t); Q4_0: C words of the unit's block 0
+  int t;
+};
+
+// ---- Q4_K: 8 sub-blocks of 32; chunk c = qs bytes 32c..32c+31, low nibbles ->
+// sub-block 2c, high -> 2c+1. Thread t takes bytes 8t..8t+7 of a chunk: A regs
+// (row g / g+8) x (bytes 8t..8t+3 = MMA k 4t..4t+3, bytes 8t+4..8t+7 = k 16+4t..),
+// matching digits stored in natural k order.
+template <int NCG, int NCC>
+__device__ __forceinline__ void unit_q4k(const Ctx& c, float (&ft)[NCG][4], float (&cmin)[2 * NCC]) {
+  const uint4 hg = lds<uint4>(c.smem, c.rg), hg8 = lds<uint4>(c.smem, c.rg8);
+  uint32_t scl[2], sch[2];
+  float dd[2], dm[2];
+  uint32_t ma[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint4 h = r == 0 ? hg : hg8;
+    dd[r] = half_bits_to_float(h.x) * 0.0625f;
+    dm[r] = half_bits_to_float(h.x >> 16);
+    // 6-bit scales / mins (gguf quants.py:479-501): sub-blocks 0..3 from bytes 0..3 / 4..7,
+    // 4..7 from the low / high nibbles of bytes 8..11 plus the top bits of bytes 0..7
+    scl[r] = h.y & 0x3F3F3F3Fu;
+    sch[r] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    const uint32_t ml = h.z & 0x3F3F3F3Fu;
+    const uint32_t mh = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    const uint32_t mw = c.t < 2 ? ml : mh;  // this thread's slots: sub-blocks 2t, 2t+1
+    const int b0 = 2 * (c.t & 1);
+    ma[r] = bf16x2_of_small(byte_of(mw, b0), byte_of(mw, b0 + 1));
+  }
+  // min part: sum_j m_j * xsum_j, cols (token, hi / lo)
+#pragma unroll
+  for (int cc = 0; cc < NCC; ++cc) {
+    float am[4];
+    mma_bf16_z(am, ma[0], ma[1], lds<uint32_t>(c.smem, c.xs + cc * 8 * 16));
+    cmin[2 * cc] = fmaf(dm[0], am[0] + am[1], cmin[2 * cc]);
+    cmin[2 * cc + 1] = fmaf(dm[1], am[2] + am[3], cmin[2 * cc + 1]);
+  }
+  int tl[NCG][4], th[NCG][4];
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    const uint2 w = lds<uint2>(c.smem, c.rg + 16u + 32u * ch + 8u * c.t);
+    const uint2 w8 = lds<uint2>(c.smem, c.rg8 + 16u + 32u * ch + 8u * c.t);
+    const uint32_t m0f = 0x0F0F0F0Fu, mf0 = 0xF0F0F0F0u;
+    const uint32_t l0 = w.x & m0f, l1 = w8.x & m0f, l2 = w.y & m0f, l3 = w8.y & m0f;
+    const uint32_t h0 = w.x & mf0, h1 = w8.x & mf0, h2 = w.y & mf0, h3 = w8.y & mf0;
+    // sub-blocks 2ch (lows) and 2ch+1 (highs): bytes of scl (ch < 2) or sch
+    const uint32_t sw = ch < 2 ? scl[0] : sch[0], sw8 = ch < 2 ? scl[1] : sch[1];
+    const int bl = 2 * (ch & 1);
+    const int sl = static_cast<int>(byte_of(sw, bl)), sl8 = static_cast<int>(byte_of(sw8, bl));
+    const int sh = static_cast<int>(byte_of(sw, bl + 1)), sh8 = static_cast<int>(byte_of(sw8, bl + 1));
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+      const uint2 xl = lds<uint2>(c.smem, c.xo[cg] + 64u * ch);
+      const uint2 xh = lds<uint2>(c.smem, c.xo[cg] + 64u * ch + 32u);
+      int al[4], ah[4];
+      imma(al, l0, l1, l2, l3, xl.x, xl.y, 0, 0, 0, 0);
+      imma(ah, h0, h1, h2, h3, xh.x, xh.y, 0, 0, 0, 0);
+      if (ch == 0) {
+        tl[cg][0] = sl * al[0]; tl[cg][1] = sl * al[1]; tl[cg][2] = sl8 * al[2]; tl[cg][3] = sl8 * al[3];
+        th[cg][0] = sh * ah[0]; th[cg][1] = sh * ah[1]; th[cg][2] = sh8 * ah[2]; th[cg][3] = sh8 * ah[3];
+      } else {
+        tl[cg][0] += sl * al[0]; tl[cg][1] += sl * al[1]; tl[cg][2] += sl8 * al[2]; tl[cg][3] += sl8 * al[3];
+        th[cg][0] += sh * ah[0]; th[cg][1] += sh * ah[1]; th[cg][2] += sh8 * ah[2]; th[cg][3] += sh8 * ah[3];
+      }
+    }
+  }
+  // lows carry q, highs 16 q: unit sum = (d / 16) * (16 tl + th); |16 tl + th| < 2^29
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg) {
+    const float2 f = lds<float2>(c.smem, c.xf + cg * 32u);
+    ft[cg][0] = fmaf(dd[0] * f.x, static_cast<float>(16 * tl[cg][0] + th[cg][0]), ft[cg][0]);
+    ft[cg][1] = fmaf(dd[0] * f.y, static_cast<float>(16 * tl[cg][1] + th[cg][1]), ft[cg][1]);
+    ft[cg][2] = fmaf(dd[1] * f.x, static_cast<float>(16 * tl[cg][2] + th[cg][2]), ft[cg][2]);
+    ft[cg][3] = fmaf(dd[1] * f.y, static_cast<float>(16 * tl[cg][3] + th[cg][3]), ft[cg][3]);
+  }
+}
+
+// ---- Q4_0: 8 blocks of 18 bytes (fp16 d + 16 nibble bytes; byte i: low -> x[i],
+// high -> x[16+i]). Thread t takes bytes 4t..4t+3 of a block: lows are MMA k
+// 4t..4t+3, highs k 16+4t..; the digits of a block are stored permuted so both
+// halves are one 8-byte load. C = -8 * (digit sums of the block, per column).
+template <int NCG>
+__device__ __forceinline__ void unit_q40(const Ctx& c, float (&ft)[NCG][4]) {
+  float fb[NCG][4];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const uint32_t og = c.rg + 18u * b, og8 = c.rg8 + 18u * b;
+    const float dg = half_bits_to_float(lds<uint16_t>(c.smem, og));
+    const float dg8 = half_bits_to_float(lds<uint16_t>(c.smem, og8));
+    // block b starts at 18b: its nibbles at 18b + 2 + 4t are 4-byte aligned for odd b
+    uint32_t w, w8;
+    if (b & 1) {
+      w = lds<uint32_t>(c.smem, og + 2u + 4u * c.t);
+      w8 = lds<uint32_t>(c.smem, og8 + 2u + 4u * c.t);
+    } else {
+      w = lds32_a2(c.smem, og + 2u + 4u * c.t);
+      w8 = lds32_a2(c.smem, og8 + 2u + 4u * c.t);
+    }
+    const uint32_t m0f = 0x0F0F0F0Fu;
+    const uint32_t a0 = w & m0f, a1 = w8 & m0f, a2 = (w >> 4) & m0f, a3 = (w8 >> 4) & m0f;
+#pragma unroll
+    for (int cg = 0; cg < NCG; ++cg) {
+      const uint2 xb = lds<uint2>(c.smem, c.xo[cg] + 32u * b);
+      const int2 cn = lds<int2>(c.smem, c.xs + (b * NCG + cg) * 32u);
+      int acc[4];
+      imma(acc, a0, a1, a2, a3, xb.x, xb.y, cn.x, cn.y, cn.x, cn.y);
+      if (b == 0) {
+        fb[cg][0] = dg * static_cast<float>(acc[0]);
+        fb[cg][1] = dg * static_cast<float>(acc[1]);
+        fb[cg][2] = dg8 * static_cast<float>(acc[2]);
+        fb[cg][3] = dg8 * static_cast<float>(acc[3]);
+      } else {
+        fb[cg][0] = fmaf(dg, static_cast<float>(acc[0]), fb[cg][0]);
+        fb[cg][1] = fmaf(dg, static_cast<float>(acc[1]), fb[cg][1]);
+        fb[cg][2] = fmaf(dg8, static_cast<float>(acc[2]), fb[cg][2]);
+        fb[cg][3] = fmaf(dg8, static_cast<float>(acc[3]), fb[cg][3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int cg = 0; cg < NCG; ++cg) {
+    const float2 f = lds<float2>(c.smem, c.xf + cg * 32u);
+    ft[cg][0] = fmaf(f.x, fb[cg][0], ft[cg][0]);
+    ft[cg][1] = fmaf(f.y, fb[cg][1], ft[cg][1]);
+    ft[cg][2] = fmaf(f.x, fb[cg][2], ft[cg][2]);
+    ft[cg][3] = fmaf(f.y, fb[cg][3], ft[cg][3]);
+  }
+}
+
+// MMA row mr (0..15) of a row block <-> weight row: with rg rows per copy the
+// row groups sit at group_pitch = 32 mod 128, and MMA rows 0..7 (one A register
+// each) take the first row of distinct groups where possible, so the 8-byte
+// reads of a quarter warp fall in distinct banks.
+__device__ __forceinline__ int phys_row(int mr, int rg) {
+  const int per = kRows / rg;
+  return rg * (mr % per) + mr / per;
+}
+__device__ __forceinline__ uint32_t row_off(int pr, const I8Args& a) {
+  return static_cast<uint32_t>((pr / a.rg) * a.group_pitch + (pr % a.rg) * a.chunk_bytes);
+}
+
+__device__ __forceinline__ const Seg& seg_of(const I8Args& a, int64_t rb) {
+  int i = 0;
+#pragma unroll
+  for (int j = 1; j < kMaxSegs; ++j)
+    if (j < a.nseg && rb >= a.seg[j].rb0) i = j;
+  return a.seg[i];
+}
+
+// Position of element e (0..31) of a Q4_0 block inside its 32 permuted digit
+// bytes: thread t's MMA k 4t..4t+3 (elements 4t..) and 16+4t.. (elements 16+4t..)
+// become bytes 8t..8t+7.
+__device__ __forceinline__ int q40_pos(int e) { return e < 16 ? (e >> 2) * 8 + (e & 3) : ((e - 16) >> 2) * 8 + 4 + (e & 3); }
+
+template <int QT, int NCG, int NCC>
+__global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.bar_off);
+  uint64_t* empty = full + a.stages;
+  uint64_t* rfull = empty + a.stages;
+  uint64_t* rempty = rfull + kRedBufs;
+  uint64_t* xiss = rempty + kRedBufs;  // the staging warps have issued their first activation loads
+  float* red = reinterpret_cast<float*>(smem + a.red_off);
+  const int64_t my_blocks = a.nrowblocks > blockIdx.x ? (a.nrowblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int64_t total_pieces = my_blocks * a.nchunks;
+  const int units = a.k / kUnitK;
+  constexpr int kDCols = 8 * NCG;  // digit columns (padded)
+  constexpr int kCCols = 8 * NCC;  // Q4_K coef columns (token, hi / lo), padded
+
+  if (tid == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kW);
+    }
+    for (int b = 0; b < kRedBufs; ++b) {
+      mbar_init(&rfull[b], kW);
+      mbar_init(&rempty[b], 1);
+    }
+    mbar_init(xiss, kW + 1);
+    fence_mbar_init();
+  }
+
+  auto issue = [&](int64_t p, int s) {
+    const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
+    const int ch = static_cast<int>(p % a.nchunks);
+    const Seg& sg = seg_of(a, rb);
+    const int64_t r0 = (rb - sg.rb0) * kRows;
+    const int nr = static_cast<int>((sg.n - r0) < kRows ? (sg.n - r0) : kRows);
+    const int nu = min(a.chunk_units, units - ch * a.chunk_units);
+    const uint32_t bytes = static_cast<uint32_t>(nu * a.unit_bytes);
+    mbar_arrive_expect_tx(&full[s], bytes * nr);
+    uint8_t* dst = smem + s * a.stage_bytes;
+    const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
+    // rg > 1 only when a chunk is the whole row: rg consecutive rows are contiguous
+    for (int r = 0, grp = 0; r < nr; r += a.rg, ++grp) {
+      const uint32_t rows = static_cast<uint32_t>(min(a.rg, nr - r));
+      bulk_g2s(dst + grp * a.group_pitch, src + r * a.row_bytes, rows * bytes, &full[s]);
+    }
+  };
+
+  __syncthreads();  // barriers initialised
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (warp == kW) {
+    // ---------------- producer ----------------
+    // Takes no part in staging x, so the back-pressure of its copies never holds
+    // up the other warps. The activations are read first: once the weight copies
+    // are queued, every other load of this SM waits behind them.
+    if (lane == 0 && mbar_wait(xiss, 0)) {
+      for (int64_t p = 0; p < total_pieces; ++p) {
+        const int s = static_cast<int>(p % a.stages);
+        if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
+        issue(p, s);
+      }
+    }
+  } else {
+    // x and y may belong to the previous kernel on the stream
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    // ---- activations -> digits. One warp per (token, unit): lane l holds x[8l..8l+7].
+    // The loads of up to kBatch tasks are issued together (one memory round trip a batch).
+    constexpr int kStagers = kW + 1, kBatch = 8;
+    const int ntask = a.m * units;
+    bool told = false;
+    for (int base = warp < kW ? warp : kW; base < ntask; base += kBatch * kStagers) {
+      uint4 raw[kBatch][2];
+#pragma unroll
+      for (int bt = 0; bt < kBatch; ++bt) {
+        const int task = base + bt * kStagers;
+        if (task < ntask) {
+          const int tok = task / units, u = task - tok * units;
+          const int64_t k0 = static_cast<int64_t>(u) * kUnitK + 8 * lane;
+          if (a.xtype == GGUFMM_F32) {
+            const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.x) + tok * a.ldx + k0);
+            raw[bt][0] = xp[0];
+            raw[bt][1] = xp[1];
+          } else {
+            raw[bt][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + tok * a.ldx + k0);
+          }
+        }
+      }
+      if (!told) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xiss);
+        told = true;
+      }
+#pragma unroll
+      for (int bt = 0; bt < kBatch; ++bt) {
+        const int task = base + bt * kStagers;
+        if (task >= ntask) break;
+        const int tok = task / units, u = task - tok * units;
+        float v[8];
+        if (a.xtype == GGUFMM_F32) {
+          const uint32_t w8[8] = {raw[bt][0].x, raw[bt][0].y, raw[bt][0].z, raw[bt][0].w,
+                                  raw[bt][1].x, raw[bt][1].y, raw[bt][1].z, raw[bt][1].w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(w8[i]);
+        } else {
+          const uint32_t w4[4] = {raw[bt][0].x, raw[bt][0].y, raw[bt][0].z, raw[bt][0].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (a.xtype == GGUFMM_BF16) {
+              v[2 * i] = __uint_as_float(w4[i] << 16);
+              v[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+            } else {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+              v[2 * i] = f.x;
+              v[2 * i + 1] = f.y;
+            }
+          }
+        }
+        float mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        // max in [2^(E-127), 2^(E-126)): inv = 2^(148-E) puts it in [2^21, 2^22); groups
+        // whose maximum is below 2^-105 (or zero) become zeros
+        const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
+        const bool live = E >= 22u && E < 255u;
+        const float inv = live ? __uint_as_float((275u - E) << 23) : 0.f;
+        const float s = live ? __uint_as_float((E - 21u) << 23) : 0.f;
+        uint32_t dg[3][2];  // [digit][word]: 8 digit bytes of this lane
+        int dsum[3] = {0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int X = __float2int_rn(v[i] * inv);
+          const int d3 = static_cast<int>(static_cast<int8_t>(X & 0xFF));
+          const int X1 = (X - d3) >> 8;
+          const int d2 = static_cast<int>(static_cast<int8_t>(X1 & 0xFF));
+          const int d1 = (X1 - d2) >> 8;
+          const int dv[3] = {d1, d2, d3};
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            const uint32_t byte = static_cast<uint32_t>(dv[j]) & 0xFFu;
+            if ((i & 3) == 0) dg[j][i >> 2] = byte;
+            else dg[j][i >> 2] |= byte << (8 * (i & 3));
+            dsum[j] += dv[j];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          uint8_t* col = smem + a.xd_off + (3 * tok + j) * a.xd_pitch + u * kUnitK;
+          if (QT == kQ4_K) {
+            *reinterpret_cast<uint2*>(col + 8 * lane) = make_uint2(dg[j][0], dg[j][1]);
+          } else {
+            // lane covers elements 8(l&3)..+7 of block l>>2: two runs of 4
+            const int e0 = 8 * (lane & 3);
+            uint8_t* blk = col + 32 * (lane >> 2);
+            *reinterpret_cast<uint32_t*>(blk + q40_pos(e0)) = dg[j][0];
+            *reinterpret_cast<uint32_t*>(blk + q40_pos(e0 + 4)) = dg[j][1];
+          }
+        }
+        if (lane < 3) {
+          const float radix = lane == 0 ? 65536.f : lane == 1 ? 256.f : 1.f;
+          reinterpret_cast<float*>(smem + a.xf_off)[u * kDCols + 3 * tok + lane] = s * radix;
+        }
+        if (QT == kQ4_K) {
+          // sums of x per 32-weight sub-block (4 lanes), as bf16 hi + lo:
+          // coef column 2 tok (hi) and 2 tok + 1 (lo), slot j = sub-block
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sum += v[i];
+          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+          if ((lane & 3) == 0) {
+            const int j = lane >> 2;
+            const __nv_bfloat16 hi = __float2bfloat16_rn(sum);
+            const __nv_bfloat16 lo = __float2bfloat16_rn(sum - __bfloat162float(hi));
+            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(smem + a.xs_off) + (u * kCCols + 2 * tok) * 8 + j;
+            e[0] = hi;
+            e[8] = lo;
+          }
+        } else {
+          // C operand of each block's MMA: -8 * (sum of the block's digits) per digit column
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 1);
+            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 2);
+          }
+          if ((lane & 3) == 0) {
+            int* cw = reinterpret_cast<int*>(smem + a.xs_off) + (u * 8 + (lane >> 2)) * kDCols + 3 * tok;
+            cw[0] = -8 * dsum[0];
+            cw[1] = -8 * dsum[1];
+            cw[2] = -8 * dsum[2];
+          }
+        }
+      }
+    }
+    if (!told && lane == 0) mbar_arrive(xiss);
+    asm volatile("bar.sync 1, %0;" ::"r"((kW + 1) * 32) : "memory");  // x staged (all but the producer)
+
+    if (warp == kW + 1) {
+      // ---------------- epilogue ----------------
+      for (int64_t blk = 0; blk < my_blocks; ++blk) {
+        const int b = static_cast<int>(blk & 1);
+        if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
+        const int64_t rb = blockIdx.x + blk * gridDim.x;
+        const float* rbuf = red + b * (kW * a.red_stride);
+        const Seg& sg = seg_of(a, rb);
+        for (int i = lane; i < kRows * a.m; i += 32) {
+          const int row = i / a.m, tok = i - row * a.m;
+          const int64_t n_idx = (rb - sg.rb0) * kRows + phys_row(row, a.rg);
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < kW; ++w) {
+            const float* rw = rbuf + w * a.red_stride;
+            v += rw[row * kDCols + 3 * tok] + rw[row * kDCols + 3 * tok + 1] + rw[row * kDCols + 3 * tok + 2];
+            if (QT == kQ4_K) v -= rw[kRows * kDCols + row * 8 + tok];
+          }
+          if (n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[b]);
+      }
+    } else {
+      // ---------------- compute ----------------
+      const int dcols = 3 * a.m, ccols = 2 * a.m;
+      uint32_t xcol[NCG];
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg) {
+        const int col = cg * 8 + g < dcols ? cg * 8 + g : 0;  // unused B columns read column 0
+        xcol[cg] = a.xd_off + col * a.xd_pitch + 8u * t;
+      }
+      const int ccol = g < ccols ? g : 0;
+      const uint32_t roff_g = row_off(phys_row(g, a.rg), a), roff_g8 = row_off(phys_row(g + 8, a.rg), a);
+      float ft[NCG][4], ft2[NCG][4];
+      float cmin[2 * NCC], cmin2[2 * NCC];
+#pragma unroll
+      for (int cg = 0; cg < NCG; ++cg)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ft[cg][i] = ft2[cg][i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2 * NCC; ++i) cmin[i] = cmin2[i] = 0.f;
+      int64_t p = 0;
+      bool ok = true;
+      for (int64_t blk = 0; blk < my_blocks && ok; ++blk) {
+        for (int ch = 0; ch < a.nchunks; ++ch, ++p) {
+          const int s = static_cast<int>(p % a.stages);
+          if (!mbar_wait(&full[s], static_cast<uint32_t>((p / a.stages) & 1))) {
+            ok = false;
+            break;
+          }
+          const int nu = min(a.chunk_units, units - ch * a.chunk_units);
+          const uint32_t sbase = static_cast<uint32_t>(s * a.stage_bytes);
+          auto ctx = [&](int uu) {
+            const int ku = ch * a.chunk_units + uu;  // unit index along K
+            Ctx c;
+            c.smem = smem;
+            c.rg = sbase + roff_g + uu * a.unit_bytes;
+            c.rg8 = sbase + roff_g8 + uu * a.unit_bytes;
+#pragma unroll
+            for (int cg = 0; cg < NCG; ++cg) c.xo[cg] = xcol[cg] + ku * kUnitK;
+            c.xf = a.xf_off + (ku * kDCols + 2 * t) * 4u;
+            if (QT == kQ4_K) c.xs = a.xs_off + ((ku * kCCols + ccol) * 8 + 2 * t) * 2u;
+            else c.xs = a.xs_off + ((ku * 8) * kDCols + 2 * t) * 4u;
+            c.t = t;
+            return c;
+          };
+          int uu = warp;
+          // two units at a time, with separate accumulators
+          for (; uu + kW < nu; uu += 2 * kW) {
+            const Ctx c0 = ctx(uu), c1 = ctx(uu + kW);
+            if (QT == kQ4_K) {
+              unit_q4k<NCG, NCC>(c0, ft, cmin);
+              unit_q4k<NCG, NCC>(c1, ft2, cmin2);
+            } else {
+              unit_q40<NCG>(c0, ft);
+              unit_q40<NCG>(c1, ft2);
+            }
+          }
+          if (uu < nu) {
+            if (QT == kQ4_K) unit_q4k<NCG, NCC>(ctx(uu), ft, cmin);
+            else unit_q40<NCG>(ctx(uu), ft);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        if (!ok) break;
+        const int b = static_cast<int>(blk & 1);
+        if (blk >= kRedBufs && !mbar_wait(&rempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
+        float* rw = red + b * (kW * a.red_stride) + warp * a.red_stride;
+#pragma unroll
+        for (int cg = 0; cg < NCG; ++cg) {
+          *reinterpret_cast<float2*>(rw + g * kDCols + cg * 8 + 2 * t) =
+              make_float2(ft[cg][0] + ft2[cg][0], ft[cg][1] + ft2[cg][1]);
+          *reinterpret_cast<float2*>(rw + (g + 8) * kDCols + cg * 8 + 2 * t) =
+              make_float2(ft[cg][2] + ft2[cg][2], ft[cg][3] + ft2[cg][3]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ft[cg][i] = ft2[cg][i] = 0.f;
+        }
+        if (QT == kQ4_K) {
+          float* rc = rw + kRows * kDCols;  // [16 rows][8 tokens]
+#pragma unroll
+          for (int cc = 0; cc < NCC; ++cc) {
+            rc[g * 8 + 4 * cc + t] = cmin[2 * cc] + cmin2[2 * cc];
+            rc[(g + 8) * 8 + 4 * cc + t] = cmin[2 * cc + 1] + cmin2[2 * cc + 1];
+          }
+#pragma unroll
+          for (int i = 0; i < 2 * NCC; ++i) cmin[i] = cmin2[i] = 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rfull[b]);
+      }
+    }
+  }
+  __syncthreads();
+  // a bounded wait may have given up: no copy of this CTA may still be in flight at exit
+  if (warp == kW && lane == 0) {
+    for (int64_t q = total_pieces - a.stages; q < total_pieces; ++q)
+      if (q >= 0) mbar_wait(&full[q % a.stages], static_cast<uint32_t>((q / a.stages) & 1));
+  }
+}
+
+int ncg_of(int m) { return (3 * m + 7) / 8; }
+
+bool plan_i8(int qt, int64_t k, int m, int smem_budget, I8Args& a) {
+  if (qt != kQ4_K && qt != kQ4_0) return false;
+  if (k % kUnitK || m < 1 || m > 8 || k > (1 << 20)) return false;
+  a.unit_bytes = 144;  // one Q4_K superblock = 8 Q4_0 blocks = 144 bytes
+  const int ncg = ncg_of(m), ncc = ncg == 1 ? 1 : 2;
+  const int units = static_cast<int>(k / kUnitK);
+  a.xd_pitch = static_cast<int>(k + 32);
+  const int xd_bytes = 3 * m * a.xd_pitch;
+  const int xf_bytes = units * 8 * ncg * 4;
+  const int xs_bytes = qt == kQ4_K ? units * 8 * ncc * 8 * 2 : units * 8 * 8 * ncg * 4;
+  a.red_stride = kRows * 8 * ncg + (qt == kQ4_K ? kRows * 8 : 0);
+  const int red_bytes = kRedBufs * kW * a.red_stride * 4;
+  const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + 17 * 8 + 64;
+  // Pieces: 16 rows x a chunk of up to 32 units (4608 bytes a row), else 16 units;
+  // copies of >= 4 KB where possible (short bulk copies are request-bound).
+  int stages = 0;
+  for (int cu_max : {32, 16}) {
+    a.chunk_units = std::min(units, cu_max);
+    a.nchunks = (units + a.chunk_units - 1) / a.chunk_units;
+    a.chunk_bytes = a.chunk_units * a.unit_bytes;
+    a.rg = 1;
+    if (a.nchunks == 1)
+      while (a.rg < 8 && 2 * a.rg * a.chunk_bytes <= kCopyBytes) a.rg *= 2;
+    a.group_pitch = (a.rg * a.chunk_bytes + 127) / 128 * 128 + 32;  // 32 mod 128: conflict-free reads
+    a.stage_bytes = (kRows / a.rg) * a.group_pitch;
+    stages = std::min(6, (smem_budget - fixed) / a.stage_bytes);
+    if (stages >= 2) break;
+  }
+  if (stages < 2) return false;
+  a.stages = stages;
+  a.xd_off = static_cast<uint32_t>(stages * a.stage_bytes);
+  a.xf_off = a.xd_off + (xd_bytes + 15) / 16 * 16;
+  a.xs_off = a.xf_off + xf_bytes;
+  a.red_off = a.xs_off + (xs_bytes + 15) / 16 * 16;
+  a.bar_off = (a.red_off + red_bytes + 7) / 8 * 8;
+  return true;
+}
+
+std::mutex g_attr_mu;
+std::set<std::pair<const void*, int>> g_attr_done;
+
+template <int QT, int NCG>
+cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
+  constexpr int NCC = NCG == 1 ? 1 : 2;
+  auto fn = gemv_i8_kernel<QT, NCG, NCC>;
+  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs + 1));
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (!g_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
+      if (e != cudaSuccess) return e;
+      g_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(a.nrowblocks, sms)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+template <int QT>
+cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
+  switch (ncg_of(a.m)) {
+    case 1: return launch_t<QT, 1>(a, dev, sms, smem_optin, st);
+    case 2: return launch_t<QT, 2>(a, dev, sms, smem_optin, st);
+    default: return launch_t<QT, 3>(a, dev, sms, smem_optin, st);
+  }
+}
+
+// GGUFMM_GEMV_IMPL=f16 turns this path off (the fp16 tensor-core GEMV then runs).
+bool i8_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GGUFMM_GEMV_IMPL");
+    return !(e && e[0] == 'f');
+  }();
+  return on;
+}
+
+}  // namespace
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+DevInfo device_info(int dev);  // capi.cu
+
+bool gemv_i8_supported(int qtype, int64_t k, int m) {
+  if (!i8_enabled()) return false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const DevInfo di = device_info(dev);
+  I8Args a{};
+  return plan_i8(qtype, k, m, std::min(di.smem_optin, 227 * 1024), a);
+}
+
+// nseg weights of one qtype and K (16-byte aligned bases, row bytes a multiple
+// of 16) against the same activations, one launch.
+cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                                   const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st) {
+  if (nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const DevInfo di = device_info(dev);
+  const int optin = std::min(di.smem_optin, 227 * 1024);
+  I8Args a{};
+  if (!plan_i8(qtype, k, static_cast<int>(m), optin, a)) return cudaErrorInvalidValue;
+  a.nseg = nseg;
+  int64_t rb = 0;
+  for (int i = 0; i < nseg; ++i) {
+    a.seg[i].q = static_cast<const uint8_t*>(q[i]);
+    a.seg[i].y = y[i];
+    a.seg[i].n = n[i];
+    a.seg[i].ldy = ldy[i];
+    a.seg[i].rb0 = rb;
+    rb += (n[i] + kRows - 1) / kRows;
+  }
+  a.nrowblocks = rb;
+  a.k = static_cast<int>(k);
+  a.row_bytes = row_bytes;
+  a.x = x;
+  a.xtype = xtype;
+  a.ldx = ldx;
+  a.m = static_cast<int>(m);
+  a.ytype = ytype;
+  if (qtype == kQ4_K) return launch_q<kQ4_K>(a, dev, di.sms, optin, st);
+  return launch_q<kQ4_0>(a, dev, di.sms, optin, st);
+}
+
+cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+
+}  // namespace ggufmm

@@ -427,21 +427,31 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
     const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
     for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
   };
-  // Weights are read-only inputs: start streaming them before anything else
-  // (and, under programmatic dependent launch, before the previous kernel on the
-  // stream has finished).
-  if (tid == 0)
-    for (int s = 0; s < a.stages && s < total_pieces; ++s) issue(s, s);
+  __syncthreads();  // barriers initialised
   // Let the next kernel on the stream begin its own prologue as SMs free up.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (warp == W) {
+    // ---------------- producer ----------------
+    // Weights are read-only inputs: the producer streams them from the start
+    // and takes no part in staging x, so the issue back-pressure of the first
+    // stages never holds up the other warps.
+    if (lane == 0) {
+      for (int64_t p = 0; p < total_pieces; ++p) {
+        const int s = static_cast<int>(p % a.stages);
+        if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
+        issue(p, s);
+      }
+    }
+  } else {
   // The activations (and the outputs) may belong to the previous kernel: wait for it.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int stid = warp < W ? tid : tid - 32;  // staging threads: all but the producer warp
 
   // activations -> permuted fp16 [cols][k]; sums per 16 / 32 weights, [k/16][8] / [k/32][8]
   {
     const int groups = a.k / 8;  // 8 consecutive k per task
     const int nparts = a.xtype == GGUFMM_F32 ? 2 : 1;
-    for (int task = tid; task < a.m * groups; task += kThreads) {
+    for (int task = stid; task < a.m * groups; task += kThreads - 32) {
       const int tok = task / groups, k0 = (task - tok * groups) * 8;
       float v[8];
       if (a.xtype == GGUFMM_F32) {
@@ -497,18 +507,9 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
       }
     }
   }
-  __syncthreads();
+  asm volatile("bar.sync 1, %0;" ::"r"(kThreads - 32) : "memory");  // x staged (all but the producer)
 
-  if (warp == W) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      for (int64_t p = a.stages; p < total_pieces; ++p) {  // pieces < stages: issued in the prologue
-        const int s = static_cast<int>(p % a.stages);
-        if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
-        issue(p, s);
-      }
-    }
-  } else if (warp == W + 1) {
+  if (warp == W + 1) {
     // ---------------- epilogue ----------------
     for (int64_t blk = 0; blk < my_blocks; ++blk) {
       const int b = static_cast<int>(blk & 1);
@@ -592,6 +593,7 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
       if (lane == 0) mbar_arrive(&rfull[b]);
     }
   }
+  }  // not the producer
   __syncthreads();
   // A bounded wait may have given up (g_device_error is set): make sure no copy
   // of this CTA is still in flight before it exits.
