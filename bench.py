@@ -275,7 +275,7 @@ def run_ours(args, rank: int, world: int) -> None:
     step_bytes = layer_bytes(m, act_bytes=2, out_bytes=4)
     value = step_bytes * steps * world / (ms / 1e3) / 1e9
 
-    # per-launch device time of the dominant kernel (every launch is gemv_mma_kernel<Q4_K>):
+    # per-launch device time of the dominant kernel (every launch is gemv_i8_kernel<Q4_K>):
     # each group alone in a CUDA graph of 30 launches over the rotating copies
     per = {}
     for grp in GROUPS:
@@ -372,7 +372,7 @@ def run_ours(args, rank: int, world: int) -> None:
                        "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
                        "graph": "CUDA graph of 3 steps", "launches_per_step": [g[0] for g in GROUPS], "parallelism": f"dp{world} (independent layer per rank)"},
             "frac_of_hbm_peak": round(value / world / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<Q4_K>", "achieved": round(achieved, 2),
+            "roofline": {"bound": "hbm", "kernel": "gemv_i8_kernel<Q4_K>", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": read_traffic("gemv_q4k_layer_m1"), "peak_source": peak_src,
                          "per_launch_us": {nm: round(v * 1e3, 2) for nm, v in per.items()}},

@@ -296,7 +296,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
   uint64_t* empty = full + a.stages;
   uint64_t* rfull = empty + a.stages;
   uint64_t* rempty = rfull + kRedBufs;
-  uint64_t* xiss = rempty + kRedBufs;  // the staging warps have issued their first activation loads
   float* red = reinterpret_cast<float*>(smem + a.red_off);
   const int64_t my_blocks = a.nrowblocks > blockIdx.x ? (a.nrowblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t total_pieces = my_blocks * a.nchunks;
@@ -313,7 +312,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
       mbar_init(&rfull[b], kW);
       mbar_init(&rempty[b], 1);
     }
-    mbar_init(xiss, kW + 1);
     fence_mbar_init();
   }
 
@@ -339,10 +337,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == kW) {
     // ---------------- producer ----------------
-    // Takes no part in staging x, so the back-pressure of its copies never holds
-    // up the other warps. The activations are read first: once the weight copies
-    // are queued, every other load of this SM waits behind them.
-    if (lane == 0 && mbar_wait(xiss, 0)) {
+    // Weights are read-only: streamed from the start (under programmatic
+    // dependent launch, before the previous kernel has finished). The producer
+    // takes no part in staging x, so the back-pressure of its copies never holds
+    // up the other warps.
+    if (lane == 0) {
       for (int64_t p = 0; p < total_pieces; ++p) {
         const int s = static_cast<int>(p % a.stages);
         if (p >= a.stages && !mbar_wait(&empty[s], static_cast<uint32_t>(((p / a.stages) - 1) & 1))) break;
@@ -357,7 +356,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
     // The loads of up to kBatch tasks are issued together (one memory round trip a batch).
     constexpr int kStagers = kW + 1, kBatch = 8;
     const int ntask = a.m * units;
-    bool told = false;
     for (int base = warp < kW ? warp : kW; base < ntask; base += kBatch * kStagers) {
       uint4 raw[kBatch][2];
 #pragma unroll
@@ -374,11 +372,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
             raw[bt][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + tok * a.ldx + k0);
           }
         }
-      }
-      if (!told) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(xiss);
-        told = true;
       }
 #pragma unroll
       for (int bt = 0; bt < kBatch; ++bt) {
@@ -483,7 +476,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
         }
       }
     }
-    if (!told && lane == 0) mbar_arrive(xiss);
     asm volatile("bar.sync 1, %0;" ::"r"((kW + 1) * 32) : "memory");  // x staged (all but the producer)
 
     if (warp == kW + 1) {
@@ -622,7 +614,7 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, I8Args& a) {
   const int xs_bytes = qt == kQ4_K ? units * 8 * ncc * 8 * 2 : units * 8 * 8 * ncg * 4;
   a.red_stride = kRows * 8 * ncg + (qt == kQ4_K ? kRows * 8 : 0);
   const int red_bytes = kRedBufs * kW * a.red_stride * 4;
-  const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + 17 * 8 + 64;
+  const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + 16 * 8 + 64;
   // Pieces: 16 rows x a chunk of up to 32 units (4608 bytes a row), else 16 units;
   // copies of >= 4 KB where possible (short bulk copies are request-bound).
   int stages = 0;
@@ -655,7 +647,7 @@ template <int QT, int NCG>
 cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   constexpr int NCC = NCG == 1 ? 1 : 2;
   auto fn = gemv_i8_kernel<QT, NCG, NCC>;
-  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs + 1));
+  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs));
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     if (!g_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
