@@ -54,8 +54,6 @@ constexpr int kUnitK = 256;
 constexpr int kCopyBytes = 4608;  // target bytes per bulk copy
 constexpr int kRedBufs = 2;
 constexpr int kMaxSegs = 4;
-constexpr int kW = 8;  // compute warps
-constexpr int kThreads = (kW + 2) * 32;
 
 struct Seg {
   const uint8_t* q;
@@ -288,8 +286,8 @@ __device__ __forceinline__ const Seg& seg_of(const I8Args& a, int64_t rb) {
 // become bytes 8t..8t+7.
 __device__ __forceinline__ int q40_pos(int e) { return e < 16 ? (e >> 2) * 8 + (e & 3) : ((e - 16) >> 2) * 8 + 4 + (e & 3); }
 
-template <int QT, int NCG, int NCC>
-__global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
+template <int QT, int NCG, int NCC, int W>
+__global__ void __launch_bounds__((W + 2) * 32, 1) gemv_i8_kernel(const I8Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.bar_off);
@@ -306,10 +304,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kW);
+      mbar_init(&empty[s], W);
     }
     for (int b = 0; b < kRedBufs; ++b) {
-      mbar_init(&rfull[b], kW);
+      mbar_init(&rfull[b], W);
       mbar_init(&rempty[b], 1);
     }
     fence_mbar_init();
@@ -335,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
 
   __syncthreads();  // barriers initialised
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  if (warp == kW) {
+  if (warp == W) {
     // ---------------- producer ----------------
     // Weights are read-only: streamed from the start (under programmatic
     // dependent launch, before the previous kernel has finished). The producer
@@ -353,83 +351,105 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // ---- activations -> digits. One warp per (token, unit): lane l holds x[8l..8l+7].
-    // The loads of up to kBatch tasks are issued together (one memory round trip a batch).
-    constexpr int kStagers = kW + 1, kBatch = 8;
+    // kB tasks of a warp go through each step together (step-major, straight-line
+    // code), so their load round trips and reduction chains overlap.
+    constexpr int kStagers = W + 1, kB = 4;
     const int ntask = a.m * units;
-    for (int base = warp < kW ? warp : kW; base < ntask; base += kBatch * kStagers) {
-      uint4 raw[kBatch][2];
+    for (int base = warp < W ? warp : W; base < ntask; base += kB * kStagers) {
+      int tok[kB], un[kB];
+      bool valid[kB];
+      uint4 raw[kB][2];
 #pragma unroll
-      for (int bt = 0; bt < kBatch; ++bt) {
+      for (int bt = 0; bt < kB; ++bt) {
         const int task = base + bt * kStagers;
-        if (task < ntask) {
-          const int tok = task / units, u = task - tok * units;
-          const int64_t k0 = static_cast<int64_t>(u) * kUnitK + 8 * lane;
-          if (a.xtype == GGUFMM_F32) {
-            const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.x) + tok * a.ldx + k0);
-            raw[bt][0] = xp[0];
-            raw[bt][1] = xp[1];
-          } else {
-            raw[bt][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + tok * a.ldx + k0);
-          }
+        valid[bt] = task < ntask;
+        const int tc = valid[bt] ? task : base;
+        tok[bt] = tc / units;
+        un[bt] = tc - tok[bt] * units;
+        const int64_t k0 = static_cast<int64_t>(un[bt]) * kUnitK + 8 * lane;
+        if (a.xtype == GGUFMM_F32) {
+          const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.x) + tok[bt] * a.ldx + k0);
+          raw[bt][0] = xp[0];
+          raw[bt][1] = xp[1];
+        } else {
+          raw[bt][0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.x) + tok[bt] * a.ldx + k0);
         }
       }
+      float v[kB][8];
+      uint32_t mxb[kB];
 #pragma unroll
-      for (int bt = 0; bt < kBatch; ++bt) {
-        const int task = base + bt * kStagers;
-        if (task >= ntask) break;
-        const int tok = task / units, u = task - tok * units;
-        float v[8];
+      for (int bt = 0; bt < kB; ++bt) {
         if (a.xtype == GGUFMM_F32) {
           const uint32_t w8[8] = {raw[bt][0].x, raw[bt][0].y, raw[bt][0].z, raw[bt][0].w,
                                   raw[bt][1].x, raw[bt][1].y, raw[bt][1].z, raw[bt][1].w};
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(w8[i]);
+          for (int i = 0; i < 8; ++i) v[bt][i] = __uint_as_float(w8[i]);
         } else {
           const uint32_t w4[4] = {raw[bt][0].x, raw[bt][0].y, raw[bt][0].z, raw[bt][0].w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (a.xtype == GGUFMM_BF16) {
-              v[2 * i] = __uint_as_float(w4[i] << 16);
-              v[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+              v[bt][2 * i] = __uint_as_float(w4[i] << 16);
+              v[bt][2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
             } else {
               const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
-              v[2 * i] = f.x;
-              v[2 * i + 1] = f.y;
+              v[bt][2 * i] = f.x;
+              v[bt][2 * i + 1] = f.y;
             }
           }
         }
         float mx = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
+        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[bt][i]));
+        // non-negative floats order like their bit patterns: one warp max
+        mxb[bt] = __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(mx));
+      }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+      for (int bt = 0; bt < kB; ++bt) {
         // max in [2^(E-127), 2^(E-126)): inv = 2^(148-E) puts it in [2^21, 2^22); groups
         // whose maximum is below 2^-105 (or zero) become zeros
-        const uint32_t E = (__float_as_uint(mx) >> 23) & 0xFFu;
+        const uint32_t E = (mxb[bt] >> 23) & 0xFFu;
         const bool live = E >= 22u && E < 255u;
         const float inv = live ? __uint_as_float((275u - E) << 23) : 0.f;
         const float s = live ? __uint_as_float((E - 21u) << 23) : 0.f;
-        uint32_t dg[3][2];  // [digit][word]: 8 digit bytes of this lane
-        int dsum[3] = {0, 0, 0};
+        // Balanced digits in one add: Y = X + 0x808080 (>= 0 as |X| <= 2^22) has the
+        // bytes d3 + 128, d2 + 128, d1 + 128, so Y ^ 0x808080 holds d3, d2, d1 as s8.
+        uint32_t z[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int X = __float2int_rn(v[i] * inv);
-          const int d3 = static_cast<int>(static_cast<int8_t>(X & 0xFF));
-          const int X1 = (X - d3) >> 8;
-          const int d2 = static_cast<int>(static_cast<int8_t>(X1 & 0xFF));
-          const int d1 = (X1 - d2) >> 8;
-          const int dv[3] = {d1, d2, d3};
-#pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            const uint32_t byte = static_cast<uint32_t>(dv[j]) & 0xFFu;
-            if ((i & 3) == 0) dg[j][i >> 2] = byte;
-            else dg[j][i >> 2] |= byte << (8 * (i & 3));
-            dsum[j] += dv[j];
-          }
-        }
+        for (int i = 0; i < 8; ++i)
+          z[i] = (static_cast<uint32_t>(__float2int_rn(v[bt][i] * inv)) + 0x808080u) ^ 0x808080u;
+        uint32_t dg[3][2];  // [digit][word]: 8 digit bytes of this lane (digit 0 = d1, the top byte)
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
-          uint8_t* col = smem + a.xd_off + (3 * tok + j) * a.xd_pitch + u * kUnitK;
+          const uint32_t b = 2u - j;  // byte of z holding digit j
+          const uint32_t sel = b | ((4u + b) << 4);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t lo = __byte_perm(z[4 * h], z[4 * h + 1], sel);
+            const uint32_t hi = __byte_perm(z[4 * h + 2], z[4 * h + 3], sel);
+            dg[j][h] = __byte_perm(lo, hi, 0x5410u);
+          }
+        }
+        float sum = 0.f;
+        int dsum[3] = {0, 0, 0};
+        if (QT == kQ4_K) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sum += v[bt][i];
+          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 3; ++j) {
+            dsum[j] = __dp4a(static_cast<int>(dg[j][0]), 0x01010101, __dp4a(static_cast<int>(dg[j][1]), 0x01010101, 0));
+            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 1);
+            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 2);
+          }
+        }
+        if (!valid[bt]) continue;
+        const int tk = tok[bt], u = un[bt];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          uint8_t* col = smem + a.xd_off + (3 * tk + j) * a.xd_pitch + u * kUnitK;
           if (QT == kQ4_K) {
             *reinterpret_cast<uint2*>(col + 8 * lane) = make_uint2(dg[j][0], dg[j][1]);
           } else {
@@ -442,33 +462,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
         }
         if (lane < 3) {
           const float radix = lane == 0 ? 65536.f : lane == 1 ? 256.f : 1.f;
-          reinterpret_cast<float*>(smem + a.xf_off)[u * kDCols + 3 * tok + lane] = s * radix;
+          reinterpret_cast<float*>(smem + a.xf_off)[u * kDCols + 3 * tk + lane] = s * radix;
         }
-        if (QT == kQ4_K) {
-          // sums of x per 32-weight sub-block (4 lanes), as bf16 hi + lo:
-          // coef column 2 tok (hi) and 2 tok + 1 (lo), slot j = sub-block
-          float sum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) sum += v[i];
-          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-          if ((lane & 3) == 0) {
+        if ((lane & 3) == 0) {
+          if (QT == kQ4_K) {
+            // sums of x per 32-weight sub-block as bf16 hi + lo: coef column 2 tok (hi)
+            // and 2 tok + 1 (lo), slot j = sub-block
             const int j = lane >> 2;
             const __nv_bfloat16 hi = __float2bfloat16_rn(sum);
             const __nv_bfloat16 lo = __float2bfloat16_rn(sum - __bfloat162float(hi));
-            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(smem + a.xs_off) + (u * kCCols + 2 * tok) * 8 + j;
+            __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(smem + a.xs_off) + (u * kCCols + 2 * tk) * 8 + j;
             e[0] = hi;
             e[8] = lo;
-          }
-        } else {
-          // C operand of each block's MMA: -8 * (sum of the block's digits) per digit column
-#pragma unroll
-          for (int j = 0; j < 3; ++j) {
-            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 1);
-            dsum[j] += __shfl_xor_sync(0xFFFFFFFFu, dsum[j], 2);
-          }
-          if ((lane & 3) == 0) {
-            int* cw = reinterpret_cast<int*>(smem + a.xs_off) + (u * 8 + (lane >> 2)) * kDCols + 3 * tok;
+          } else {
+            // C operand of each block's MMA: -8 * (sum of the block's digits) per digit column
+            int* cw = reinterpret_cast<int*>(smem + a.xs_off) + (u * 8 + (lane >> 2)) * kDCols + 3 * tk;
             cw[0] = -8 * dsum[0];
             cw[1] = -8 * dsum[1];
             cw[2] = -8 * dsum[2];
@@ -476,27 +484,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
         }
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"((kW + 1) * 32) : "memory");  // x staged (all but the producer)
+    asm volatile("bar.sync 1, %0;" ::"r"((W + 1) * 32) : "memory");  // x staged (all but the producer)
 
-    if (warp == kW + 1) {
+    if (warp == W + 1) {
       // ---------------- epilogue ----------------
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
         const int b = static_cast<int>(blk & 1);
         if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
         const int64_t rb = blockIdx.x + blk * gridDim.x;
-        const float* rbuf = red + b * (kW * a.red_stride);
+        const float* rbuf = red + b * (W * a.red_stride);
         const Seg& sg = seg_of(a, rb);
-        for (int i = lane; i < kRows * a.m; i += 32) {
-          const int row = i / a.m, tok = i - row * a.m;
-          const int64_t n_idx = (rb - sg.rb0) * kRows + phys_row(row, a.rg);
+        // lane = (row, half): rows on consecutive lanes read consecutive words of
+        // the column-major partials (no bank conflicts); each half sums W/2 warps
+        for (int i = lane; i < 32 * a.m; i += 32) {
+          const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
           float v = 0.f;
 #pragma unroll
-          for (int w = 0; w < kW; ++w) {
+          for (int w = half * (W / 2); w < (half + 1) * (W / 2); ++w) {
             const float* rw = rbuf + w * a.red_stride;
-            v += rw[row * kDCols + 3 * tok] + rw[row * kDCols + 3 * tok + 1] + rw[row * kDCols + 3 * tok + 2];
-            if (QT == kQ4_K) v -= rw[kRows * kDCols + row * 8 + tok];
+            v += rw[(3 * tok) * kRows + row] + rw[(3 * tok + 1) * kRows + row] + rw[(3 * tok + 2) * kRows + row];
+            if (QT == kQ4_K) v -= rw[kRows * kDCols + tok * kRows + row];
           }
-          if (n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
+          v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
+          const int64_t n_idx = (rb - sg.rb0) * kRows + phys_row(row, a.rg);
+          if (half == 0 && n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[b]);
@@ -547,8 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
           };
           int uu = warp;
           // two units at a time, with separate accumulators
-          for (; uu + kW < nu; uu += 2 * kW) {
-            const Ctx c0 = ctx(uu), c1 = ctx(uu + kW);
+          for (; W == 8 && uu + W < nu; uu += 2 * W) {
+            const Ctx c0 = ctx(uu), c1 = ctx(uu + W);
             if (QT == kQ4_K) {
               unit_q4k<NCG, NCC>(c0, ft, cmin);
               unit_q4k<NCG, NCC>(c1, ft2, cmin2);
@@ -557,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
               unit_q40<NCG>(c1, ft2);
             }
           }
-          if (uu < nu) {
+          for (; uu < nu; uu += W) {
             if (QT == kQ4_K) unit_q4k<NCG, NCC>(ctx(uu), ft, cmin);
             else unit_q40<NCG>(ctx(uu), ft);
           }
@@ -567,22 +578,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
         if (!ok) break;
         const int b = static_cast<int>(blk & 1);
         if (blk >= kRedBufs && !mbar_wait(&rempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
-        float* rw = red + b * (kW * a.red_stride) + warp * a.red_stride;
+        float* rw = red + b * (W * a.red_stride) + warp * a.red_stride;
 #pragma unroll
-        for (int cg = 0; cg < NCG; ++cg) {
-          *reinterpret_cast<float2*>(rw + g * kDCols + cg * 8 + 2 * t) =
-              make_float2(ft[cg][0] + ft2[cg][0], ft[cg][1] + ft2[cg][1]);
-          *reinterpret_cast<float2*>(rw + (g + 8) * kDCols + cg * 8 + 2 * t) =
-              make_float2(ft[cg][2] + ft2[cg][2], ft[cg][3] + ft2[cg][3]);
+        for (int cg = 0; cg < NCG; ++cg) {  // column-major [col][16 rows]
+          const int c0 = cg * 8 + 2 * t;
+          rw[c0 * kRows + g] = ft[cg][0] + ft2[cg][0];
+          rw[(c0 + 1) * kRows + g] = ft[cg][1] + ft2[cg][1];
+          rw[c0 * kRows + g + 8] = ft[cg][2] + ft2[cg][2];
+          rw[(c0 + 1) * kRows + g + 8] = ft[cg][3] + ft2[cg][3];
 #pragma unroll
           for (int i = 0; i < 4; ++i) ft[cg][i] = ft2[cg][i] = 0.f;
         }
         if (QT == kQ4_K) {
-          float* rc = rw + kRows * kDCols;  // [16 rows][8 tokens]
+          float* rc = rw + kRows * kDCols;  // [8 tokens][16 rows]
 #pragma unroll
           for (int cc = 0; cc < NCC; ++cc) {
-            rc[g * 8 + 4 * cc + t] = cmin[2 * cc] + cmin2[2 * cc];
-            rc[(g + 8) * 8 + 4 * cc + t] = cmin[2 * cc + 1] + cmin2[2 * cc + 1];
+            rc[(4 * cc + t) * kRows + g] = cmin[2 * cc] + cmin2[2 * cc];
+            rc[(4 * cc + t) * kRows + g + 8] = cmin[2 * cc + 1] + cmin2[2 * cc + 1];
           }
 #pragma unroll
           for (int i = 0; i < 2 * NCC; ++i) cmin[i] = cmin2[i] = 0.f;
@@ -594,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
   }
   __syncthreads();
   // a bounded wait may have given up: no copy of this CTA may still be in flight at exit
-  if (warp == kW && lane == 0) {
+  if (warp == W && lane == 0) {
     for (int64_t q = total_pieces - a.stages; q < total_pieces; ++q)
       if (q >= 0) mbar_wait(&full[q % a.stages], static_cast<uint32_t>((q / a.stages) & 1));
   }
@@ -602,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_i8_kernel(const I8Args a) {
 
 int ncg_of(int m) { return (3 * m + 7) / 8; }
 
-bool plan_i8(int qt, int64_t k, int m, int smem_budget, I8Args& a) {
+bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, I8Args& a) {
   if (qt != kQ4_K && qt != kQ4_0) return false;
   if (k % kUnitK || m < 1 || m > 8 || k > (1 << 20)) return false;
   a.unit_bytes = 144;  // one Q4_K superblock = 8 Q4_0 blocks = 144 bytes
@@ -612,8 +624,9 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, I8Args& a) {
   const int xd_bytes = 3 * m * a.xd_pitch;
   const int xf_bytes = units * 8 * ncg * 4;
   const int xs_bytes = qt == kQ4_K ? units * 8 * ncc * 8 * 2 : units * 8 * 8 * ncg * 4;
-  a.red_stride = kRows * 8 * ncg + (qt == kQ4_K ? kRows * 8 : 0);
-  const int red_bytes = kRedBufs * kW * a.red_stride * 4;
+  // + 4 floats: the two halves of the epilogue warp (4 or 8 warps apart) hit different banks
+  a.red_stride = kRows * 8 * ncg + (qt == kQ4_K ? kRows * 8 : 0) + 4;
+  const int red_bytes = kRedBufs * W * a.red_stride * 4;
   const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + 16 * 8 + 64;
   // Pieces: 16 rows x a chunk of up to 32 units (4608 bytes a row), else 16 units;
   // copies of >= 4 KB where possible (short bulk copies are request-bound).
@@ -643,10 +656,10 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, I8Args& a) {
 std::mutex g_attr_mu;
 std::set<std::pair<const void*, int>> g_attr_done;
 
-template <int QT, int NCG>
+template <int QT, int NCG, int W>
 cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   constexpr int NCC = NCG == 1 ? 1 : 2;
-  auto fn = gemv_i8_kernel<QT, NCG, NCC>;
+  auto fn = gemv_i8_kernel<QT, NCG, NCC, W>;
   const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs));
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
@@ -658,7 +671,7 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(a.nrowblocks, sms)));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3((W + 2) * 32);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -669,13 +682,22 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
-template <int QT>
+template <int QT, int W>
 cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   switch (ncg_of(a.m)) {
-    case 1: return launch_t<QT, 1>(a, dev, sms, smem_optin, st);
-    case 2: return launch_t<QT, 2>(a, dev, sms, smem_optin, st);
-    default: return launch_t<QT, 3>(a, dev, sms, smem_optin, st);
+    case 1: return launch_t<QT, 1, W>(a, dev, sms, smem_optin, st);
+    case 2: return launch_t<QT, 2, W>(a, dev, sms, smem_optin, st);
+    default: return launch_t<QT, 3, W>(a, dev, sms, smem_optin, st);
   }
+}
+
+// Compute warps per CTA: 8 (GGUFMM_GEMV_WARPS=16 for tuning).
+int i8_warps() {
+  static const int w = [] {
+    const char* e = std::getenv("GGUFMM_GEMV_WARPS");
+    return e && std::atoi(e) == 16 ? 16 : 8;
+  }();
+  return w;
 }
 
 // GGUFMM_GEMV_IMPL=f16 turns this path off (the fp16 tensor-core GEMV then runs).
@@ -701,7 +723,7 @@ bool gemv_i8_supported(int qtype, int64_t k, int m) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const DevInfo di = device_info(dev);
   I8Args a{};
-  return plan_i8(qtype, k, m, std::min(di.smem_optin, 227 * 1024), a);
+  return plan_i8(qtype, k, m, std::min(di.smem_optin, 227 * 1024), i8_warps(), a);
 }
 
 // nseg weights of one qtype and K (16-byte aligned bases, row bytes a multiple
@@ -716,7 +738,8 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   const DevInfo di = device_info(dev);
   const int optin = std::min(di.smem_optin, 227 * 1024);
   I8Args a{};
-  if (!plan_i8(qtype, k, static_cast<int>(m), optin, a)) return cudaErrorInvalidValue;
+  const int W = i8_warps();
+  if (!plan_i8(qtype, k, static_cast<int>(m), optin, W, a)) return cudaErrorInvalidValue;
   a.nseg = nseg;
   int64_t rb = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -735,8 +758,9 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   a.ldx = ldx;
   a.m = static_cast<int>(m);
   a.ytype = ytype;
-  if (qtype == kQ4_K) return launch_q<kQ4_K>(a, dev, di.sms, optin, st);
-  return launch_q<kQ4_0>(a, dev, di.sms, optin, st);
+  if (W == 8) return qtype == kQ4_K ? launch_q<kQ4_K, 8>(a, dev, di.sms, optin, st)
+                                    : launch_q<kQ4_0, 8>(a, dev, di.sms, optin, st);
+  return qtype == kQ4_K ? launch_q<kQ4_K, 16>(a, dev, di.sms, optin, st) : launch_q<kQ4_0, 16>(a, dev, di.sms, optin, st);
 }
 
 cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
