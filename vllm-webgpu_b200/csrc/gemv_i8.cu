@@ -287,7 +287,7 @@ __device__ __forceinline__ const Seg& seg_of(const I8Args& a, int64_t rb) {
 __device__ __forceinline__ int q40_pos(int e) { return e < 16 ? (e >> 2) * 8 + (e & 3) : ((e - 16) >> 2) * 8 + 4 + (e & 3); }
 
 template <int QT, int NCG, int NCC, int W>
-__global__ void __launch_bounds__((W + 2) * 32, 1) gemv_i8_kernel(const I8Args a) {
+__global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(const I8Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.bar_off);
@@ -558,7 +558,7 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_i8_kernel(const I8Args a
           };
           int uu = warp;
           // two units at a time, with separate accumulators
-          for (; W == 8 && uu + W < nu; uu += 2 * W) {
+          for (; W <= 8 && uu + W < nu; uu += 2 * W) {
             const Ctx c0 = ctx(uu), c1 = ctx(uu + W);
             if (QT == kQ4_K) {
               unit_q4k<NCG, NCC>(c0, ft, cmin);
@@ -691,13 +691,25 @@ cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
   }
 }
 
-// Compute warps per CTA: 8 (GGUFMM_GEMV_WARPS=16 for tuning).
-int i8_warps() {
+// CTA shape: 4 compute warps in <= 113 KB of shared memory, two CTAs per SM
+// (the next launch's CTAs become resident, and start streaming their weights,
+// as soon as any CTA of the previous one exits), when the activations and two
+// ring stages fit; else 8 compute warps, one CTA per SM. GGUFMM_GEMV_WARPS=8 or
+// 16 forces the one-CTA shape (tuning).
+int forced_warps() {
   static const int w = [] {
     const char* e = std::getenv("GGUFMM_GEMV_WARPS");
-    return e && std::atoi(e) == 16 ? 16 : 8;
+    const int v = e ? std::atoi(e) : 0;
+    return v == 16 || v == 8 ? v : 0;
   }();
   return w;
+}
+int smem_of(int W, int optin) { return std::min(optin, W == 4 ? 113 * 1024 : 227 * 1024); }
+int pick_warps(int qt, int64_t k, int m, int optin, I8Args& a) {
+  const int f = forced_warps();
+  if (f) return plan_i8(qt, k, m, smem_of(f, optin), f, a) ? f : 0;
+  if (plan_i8(qt, k, m, smem_of(4, optin), 4, a)) return 4;
+  return plan_i8(qt, k, m, smem_of(8, optin), 8, a) ? 8 : 0;
 }
 
 // GGUFMM_GEMV_IMPL=f16 turns this path off (the fp16 tensor-core GEMV then runs).
@@ -723,7 +735,7 @@ bool gemv_i8_supported(int qtype, int64_t k, int m) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const DevInfo di = device_info(dev);
   I8Args a{};
-  return plan_i8(qtype, k, m, std::min(di.smem_optin, 227 * 1024), i8_warps(), a);
+  return pick_warps(qtype, k, m, di.smem_optin, a) != 0;
 }
 
 // nseg weights of one qtype and K (16-byte aligned bases, row bytes a multiple
@@ -736,10 +748,10 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const DevInfo di = device_info(dev);
-  const int optin = std::min(di.smem_optin, 227 * 1024);
   I8Args a{};
-  const int W = i8_warps();
-  if (!plan_i8(qtype, k, static_cast<int>(m), optin, W, a)) return cudaErrorInvalidValue;
+  const int W = pick_warps(qtype, k, static_cast<int>(m), di.smem_optin, a);
+  if (!W) return cudaErrorInvalidValue;
+  const int optin = smem_of(W, di.smem_optin);
   a.nseg = nseg;
   int64_t rb = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -758,6 +770,8 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   a.ldx = ldx;
   a.m = static_cast<int>(m);
   a.ytype = ytype;
+  if (W == 4) return qtype == kQ4_K ? launch_q<kQ4_K, 4>(a, dev, 2 * di.sms, optin, st)
+                                    : launch_q<kQ4_0, 4>(a, dev, 2 * di.sms, optin, st);
   if (W == 8) return qtype == kQ4_K ? launch_q<kQ4_K, 8>(a, dev, di.sms, optin, st)
                                     : launch_q<kQ4_0, 8>(a, dev, di.sms, optin, st);
   return qtype == kQ4_K ? launch_q<kQ4_K, 16>(a, dev, di.sms, optin, st) : launch_q<kQ4_0, 16>(a, dev, di.sms, optin, st);
