@@ -353,7 +353,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     // ---- activations -> digits. One warp per (token, unit): lane l holds x[8l..8l+7].
     // kB tasks of a warp go through each step together (step-major, straight-line
     // code), so their load round trips and reduction chains overlap.
-    constexpr int kStagers = W + 1, kB = 4;
+    constexpr int kStagers = W + 1, kB = W == 8 ? 8 : 4;
     const int ntask = a.m * units;
     for (int base = warp < W ? warp : W; base < ntask; base += kB * kStagers) {
       int tok[kB], un[kB];
