@@ -84,12 +84,46 @@ struct I8Args {
   int64_t nrowblocks;
   int xd_pitch;      // bytes per digit column of x
   int red_stride;    // floats per warp in one reduction buffer
+  int ksplit;        // 1, or 2: K halves on the two CTAs of a cluster, partials joined in rank 0
   uint32_t xd_off;   // int8 digits [3m cols][k]
   uint32_t xf_off;   // float fold factors [unit][8 NCG cols]: s * radix
   uint32_t xs_off;   // Q4_K: bf16 x sums [unit][8 NCC cols][8 sub-blocks]; Q4_0: int -8*digit sums [block][8 NCG cols]
   uint32_t red_off;
+  uint32_t xchg_off;  // ksplit 2: [2 slots][8 tokens][16 rows] floats of rank 1's partials, in rank 0
   uint32_t bar_off;
 };
+
+// ---- cluster (distributed shared memory) helpers for the K split ----
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (i > 256) __nanosleep(64);
+  }
+  atomicOr(&g_device_error, kErrWaitTimeout);
+  return false;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 __device__ __forceinline__ void imma(int* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                      uint32_t b1, int c0, int c1, int c2, int c3) {
@@ -294,10 +328,16 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   uint64_t* empty = full + a.stages;
   uint64_t* rfull = empty + a.stages;
   uint64_t* rempty = rfull + kRedBufs;
+  uint64_t* xfull = rempty + kRedBufs;  // ksplit 2, rank 0: rank 1's partials of a slot have landed
+  uint64_t* xempty = xfull + 2;         // ksplit 2, rank 1: rank 0 has consumed a slot
   float* red = reinterpret_cast<float*>(smem + a.red_off);
-  const int64_t my_blocks = a.nrowblocks > blockIdx.x ? (a.nrowblocks - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // with the K split, the two CTAs of a cluster (consecutive blockIdx.x) share row blocks
+  const int rank = a.ksplit == 2 ? static_cast<int>(blockIdx.x & 1) : 0;
+  const int64_t cid = blockIdx.x / a.ksplit, ncl = gridDim.x / a.ksplit;
+  const int64_t my_blocks = a.nrowblocks > cid ? (a.nrowblocks - 1 - cid) / ncl + 1 : 0;
   const int64_t total_pieces = my_blocks * a.nchunks;
-  const int units = a.k / kUnitK;
+  const int units = a.k / kUnitK / a.ksplit;  // this CTA's units along K
+  const int ku0 = rank * units;                // ... starting here
   constexpr int kDCols = 8 * NCG;  // digit columns (padded)
   constexpr int kCCols = 8 * NCC;  // Q4_K coef columns (token, hi / lo), padded
 
@@ -310,11 +350,15 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
       mbar_init(&rfull[b], W);
       mbar_init(&rempty[b], 1);
     }
+    mbar_init(&xfull[0], 1);
+    mbar_init(&xfull[1], 1);
+    mbar_init(&xempty[0], 1);
+    mbar_init(&xempty[1], 1);
     fence_mbar_init();
   }
 
   auto issue = [&](int64_t p, int s) {
-    const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
+    const int64_t rb = cid + (p / a.nchunks) * ncl;
     const int ch = static_cast<int>(p % a.nchunks);
     const Seg& sg = seg_of(a, rb);
     const int64_t r0 = (rb - sg.rb0) * kRows;
@@ -323,8 +367,9 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     const uint32_t bytes = static_cast<uint32_t>(nu * a.unit_bytes);
     mbar_arrive_expect_tx(&full[s], bytes * nr);
     uint8_t* dst = smem + s * a.stage_bytes;
-    const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
-    // rg > 1 only when a chunk is the whole row: rg consecutive rows are contiguous
+    const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ku0) * a.unit_bytes +
+                         static_cast<int64_t>(ch) * a.chunk_bytes;
+    // rg > 1 only when a chunk is the whole row (one chunk, no K split): rg consecutive rows are contiguous
     for (int r = 0, grp = 0; r < nr; r += a.rg, ++grp) {
       const uint32_t rows = static_cast<uint32_t>(min(a.rg, nr - r));
       bulk_g2s(dst + grp * a.group_pitch, src + r * a.row_bytes, rows * bytes, &full[s]);
@@ -332,6 +377,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   };
 
   __syncthreads();  // barriers initialised
+  if (a.ksplit == 2) cluster_sync_all();  // ... in both CTAs of the cluster before any remote arrive
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == W) {
     // ---------------- producer ----------------
@@ -366,7 +412,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
         const int tc = valid[bt] ? task : base;
         tok[bt] = tc / units;
         un[bt] = tc - tok[bt] * units;
-        const int64_t k0 = static_cast<int64_t>(un[bt]) * kUnitK + 8 * lane;
+        const int64_t k0 = static_cast<int64_t>(ku0 + un[bt]) * kUnitK + 8 * lane;
         if (a.xtype == GGUFMM_F32) {
           const uint4* xp = reinterpret_cast<const uint4*>(static_cast<const float*>(a.x) + tok[bt] * a.ldx + k0);
           raw[bt][0] = xp[0];
@@ -491,9 +537,12 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
         const int b = static_cast<int>(blk & 1);
         if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
-        const int64_t rb = blockIdx.x + blk * gridDim.x;
+        const int64_t rb = cid + blk * ncl;
         const float* rbuf = red + b * (W * a.red_stride);
         const Seg& sg = seg_of(a, rb);
+        float* xslot = reinterpret_cast<float*>(smem + a.xchg_off) + b * (8 * kRows);
+        if (rank == 1 && blk >= 2 && !mbar_wait_cluster(&xempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
+        if (rank == 0 && a.ksplit == 2 && !mbar_wait_cluster(&xfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
         // lane = (row, half): rows on consecutive lanes read consecutive words of
         // the column-major partials (no bank conflicts); each half sums W/2 warps
         for (int i = lane; i < 32 * a.m; i += 32) {
@@ -507,7 +556,21 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
           }
           v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
           const int64_t n_idx = (rb - sg.rb0) * kRows + phys_row(row, a.rg);
-          if (half == 0 && n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
+          if (rank == 1) {
+            // this CTA's K half goes to rank 0, which adds it and stores y
+            if (half == 0) st_cluster_f32(cluster_addr(xslot + tok * kRows + row, 0), v);
+          } else {
+            if (a.ksplit == 2) v += xslot[tok * kRows + row];
+            if (half == 0 && n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
+          }
+        }
+        if (rank == 1) {
+          asm volatile("fence.acq_rel.cluster;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(cluster_addr(&xfull[b], 0));
+        } else if (a.ksplit == 2) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(cluster_addr(&xempty[b], 1));
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[b]);
@@ -605,6 +668,8 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     }
   }
   __syncthreads();
+  // neither CTA of a cluster leaves while the other may still touch its shared memory
+  if (a.ksplit == 2) cluster_sync_all();
   // a bounded wait may have given up: no copy of this CTA may still be in flight at exit
   if (warp == W && lane == 0) {
     for (int64_t q = total_pieces - a.stages; q < total_pieces; ++q)
@@ -614,20 +679,23 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
 
 int ncg_of(int m) { return (3 * m + 7) / 8; }
 
-bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, I8Args& a) {
+bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, int ksplit, I8Args& a) {
   if (qt != kQ4_K && qt != kQ4_0) return false;
   if (k % kUnitK || m < 1 || m > 8 || k > (1 << 20)) return false;
+  if (k % (ksplit * kUnitK)) return false;
+  a.ksplit = ksplit;
   a.unit_bytes = 144;  // one Q4_K superblock = 8 Q4_0 blocks = 144 bytes
   const int ncg = ncg_of(m), ncc = ncg == 1 ? 1 : 2;
-  const int units = static_cast<int>(k / kUnitK);
-  a.xd_pitch = static_cast<int>(k + 32);
+  const int units = static_cast<int>(k / kUnitK) / ksplit;  // per CTA
+  a.xd_pitch = units * kUnitK + 32;
   const int xd_bytes = 3 * m * a.xd_pitch;
   const int xf_bytes = units * 8 * ncg * 4;
   const int xs_bytes = qt == kQ4_K ? units * 8 * ncc * 8 * 2 : units * 8 * 8 * ncg * 4;
   // + 4 floats: the two halves of the epilogue warp (4 or 8 warps apart) hit different banks
   a.red_stride = kRows * 8 * ncg + (qt == kQ4_K ? kRows * 8 : 0) + 4;
   const int red_bytes = kRedBufs * W * a.red_stride * 4;
-  const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + 16 * 8 + 64;
+  const int xchg_bytes = ksplit == 2 ? 2 * 8 * kRows * 4 : 0;
+  const int fixed = xd_bytes + xf_bytes + xs_bytes + red_bytes + xchg_bytes + 20 * 8 + 64;
   // Pieces: 16 rows x a chunk of up to 32 units (4608 bytes a row), else 16 units;
   // copies of >= 4 KB where possible (short bulk copies are request-bound).
   int stages = 0;
@@ -636,7 +704,7 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, I8Args& a) {
     a.nchunks = (units + a.chunk_units - 1) / a.chunk_units;
     a.chunk_bytes = a.chunk_units * a.unit_bytes;
     a.rg = 1;
-    if (a.nchunks == 1)
+    if (a.nchunks == 1 && ksplit == 1)  // rows contiguous only when a chunk is the whole row
       while (a.rg < 8 && 2 * a.rg * a.chunk_bytes <= kCopyBytes) a.rg *= 2;
     a.group_pitch = (a.rg * a.chunk_bytes + 127) / 128 * 128 + 32;  // 32 mod 128: conflict-free reads
     a.stage_bytes = (kRows / a.rg) * a.group_pitch;
@@ -649,7 +717,8 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, I8Args& a) {
   a.xf_off = a.xd_off + (xd_bytes + 15) / 16 * 16;
   a.xs_off = a.xf_off + xf_bytes;
   a.red_off = a.xs_off + (xs_bytes + 15) / 16 * 16;
-  a.bar_off = (a.red_off + red_bytes + 7) / 8 * 8;
+  a.xchg_off = a.red_off + red_bytes;
+  a.bar_off = (a.xchg_off + xchg_bytes + 7) / 8 * 8;
   return true;
 }
 
@@ -660,7 +729,7 @@ template <int QT, int NCG, int W>
 cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   constexpr int NCC = NCG == 1 ? 1 : 2;
   auto fn = gemv_i8_kernel<QT, NCG, NCC, W>;
-  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs));
+  const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs + 4));
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
     if (!g_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
@@ -670,15 +739,20 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(a.nrowblocks, sms)));
+  // sms = CTA slots; with the K split a cluster of 2 takes two of them
+  cfg.gridDim = dim3(static_cast<unsigned>(a.ksplit * std::min<int64_t>(a.nrowblocks, sms / a.ksplit)));
   cfg.blockDim = dim3((W + 2) * 32);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.ksplit;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = a.ksplit == 2 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
@@ -704,12 +778,21 @@ int forced_warps() {
   }();
   return w;
 }
+bool ksplit_disabled() {
+  static const bool off = [] {
+    const char* e = std::getenv("GGUFMM_GEMV_KSPLIT");
+    return e && e[0] == '0';
+  }();
+  return off;
+}
 int smem_of(int W, int optin) { return std::min(optin, W == 4 ? 113 * 1024 : 227 * 1024); }
 int pick_warps(int qt, int64_t k, int m, int optin, I8Args& a) {
   const int f = forced_warps();
-  if (f) return plan_i8(qt, k, m, smem_of(f, optin), f, a) ? f : 0;
-  if (plan_i8(qt, k, m, smem_of(4, optin), 4, a)) return 4;
-  return plan_i8(qt, k, m, smem_of(8, optin), 8, a) ? 8 : 0;
+  if (f) return plan_i8(qt, k, m, smem_of(f, optin), f, 1, a) ? f : 0;
+  if (plan_i8(qt, k, m, smem_of(4, optin), 4, 1, a)) return 4;
+  // too large for one half-SM CTA: split K over the two CTAs of a cluster
+  if (!ksplit_disabled() && plan_i8(qt, k, m, smem_of(4, optin), 4, 2, a)) return 4;
+  return plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a) ? 8 : 0;
 }
 
 // GGUFMM_GEMV_IMPL=f16 turns this path off (the fp16 tensor-core GEMV then runs).
