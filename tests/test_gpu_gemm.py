@@ -51,6 +51,13 @@ def test_gemm_prefill_config(cuda, qt, m):
     assert _check(qt, m, 14336, 4096, rows=384) <= TOL
 
 
+@pytest.mark.parametrize("qt", [O.Q4_K, O.Q8_0], ids=lambda q: QNAMES[q])
+def test_gemm_many_tiles_per_cta_ragged(cuda, qt):
+    """785 tiles (5 token tiles x 157 weight tiles, both ragged): several tiles per
+    CTA of the persistent GEMM, both TMEM accumulators reused."""
+    assert _check(qt, 1100, 20000, 512, rows=512) <= TOL
+
+
 def test_gemm_prefill_8192_sampled(cuda):
     assert _check(O.Q4_K, 8192, 14336, 4096, rows=128) <= TOL
 

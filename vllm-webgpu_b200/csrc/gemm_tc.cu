@@ -22,6 +22,7 @@
 //               fly, coalesced stores of Y.
 // Every TMA load is a plain (single-CTA) load of this GPU's own memory.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -36,7 +37,7 @@ struct GemmSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStageBytes;
-  static constexpr uint32_t kTotal = kBarOff + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t kTotal = kBarOff + (2 * STAGES + 6) * 8 + 16 + 1024;  // + alignment slack
 };
 
 template <int BN, int STAGES>
@@ -142,17 +143,151 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Persistent variant: one CTA per SM walks the tiles (token tiles fastest) and
+// keeps TWO accumulators in TMEM (2 x BN columns), so the epilogue warps drain
+// tile i while the MMA warp already accumulates tile i+1, and TMEM allocation,
+// barrier set-up and pipeline fill are paid once per CTA instead of per tile.
+//   tfull[b]   MMA warp -> epilogue: accumulator b holds a finished tile
+//   tempty[b]  epilogue (4 warps) -> MMA warp: accumulator b has been read
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                              void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtiles = (m + BN - 1) / BN, ntiles = (n + kTileW - 1) / kTileW;
+  const int tiles = mtiles * ntiles;
+  const int nk = (k + kBK - 1) / kBK;
+  const int my_tiles = tiles > static_cast<int>(blockIdx.x) ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int q = 0;  // running k-block index over all of this CTA's tiles
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        const int m0 = (t % mtiles) * BN, n0 = (t / mtiles) * kTileW;
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int s = q % STAGES;
+          if (!mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a_dst = smem + s * L::kStageBytes;
+          uint8_t* b_dst = a_dst + L::kABytes;
+          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          tma_load_2d(a_dst, &tmap_w, kb * kBK, n0, &full[s]);
+          tma_load_2d(b_dst, &tmap_x, kb * kBK, m0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16<BN>();
+      int q = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait(&tempty[b], static_cast<uint32_t>(((i >> 1) - 1) & 1))) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem_d + static_cast<uint32_t>(b * BN);
+        for (int kb = 0; kb < nk; ++kb, ++q) {
+          const int s = q % STAGES;
+          if (!mbar_wait(&full[s], (q / STAGES) & 1)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+          const uint64_t adesc = umma_smem_desc(a_addr), bdesc = umma_smem_desc(b_addr);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[b]);  // this tile's MMAs complete -> accumulator b ready
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM lanes 32*(warp%4) .. +31 = weight rows
+    const int quad = warp & 3;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i & 1;
+      const int t = blockIdx.x + i * gridDim.x;
+      const int m0 = (t % mtiles) * BN, n0 = (t / mtiles) * kTileW;
+      if (!mbar_wait(&tfull[b], static_cast<uint32_t>((i >> 1) & 1))) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int nrow = n0 + quad * 32 + lane;
+      const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(b * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c0, r);
+        if (nrow < n) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int mm = m0 + c0 + j;
+            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(2 * BN) : "memory");
+  }
+}
+
 // ---- host side --------------------------------------------------------------
 static std::mutex g_gemm_attr_mu;
 static std::set<std::pair<const void*, int>> g_gemm_attr_done;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PERSIST = false>
 static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
                                   int ytype, int64_t ldy, cudaStream_t st) {
   using L = GemmSmem<BN, STAGES>;
   CUtensorMap mw, mx;
   if (!make_map_f16(&mw, w16, n, k, kTileW) || !make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
-  auto fn = gemm_tc_kernel<BN, STAGES>;
+  auto fn = PERSIST ? gemm_tc_persistent_kernel<BN, STAGES> : gemm_tc_kernel<BN, STAGES>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -165,6 +300,12 @@ static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, i
     }
   }
   dim3 grid(static_cast<unsigned>((m + BN - 1) / BN), static_cast<unsigned>((n + kTileW - 1) / kTileW));
+  if (PERSIST) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    grid = dim3(static_cast<unsigned>(std::min<int64_t>(static_cast<int64_t>(grid.x) * grid.y, sms)));
+  }
   fn<<<grid, 192, L::kTotal, st>>>(mw, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
                                    static_cast<int>(k));
   return cudaGetLastError();
@@ -179,6 +320,11 @@ cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t
   if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
   if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
   if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st);
+  static const bool persist = [] {
+    const char* e = std::getenv("GGUFMM_GEMM_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  if (persist) return launch_gemm_bn<256, 4, true>(w16, x16, n, m, k, y, ytype, ldy, st);
   return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st);
 }
 
