@@ -108,9 +108,15 @@ __device__ __forceinline__ void dequant32<kQ4_K>(const uint8_t* row, int unit, f
   ldg_words_a2<8>(b + 16 + 32 * (j >> 1), w);
   const int sh = 4 * (j & 1);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    uint32_t q = (byte_of(w, i) >> sh) & 15u;
-    o[i] = __fsub_rn(__fmul_rn(dsc, small_int_to_float(static_cast<int>(q))), dm);
+  for (int i = 0; i < 8; ++i) {
+    // four nibbles at once; each becomes the float 2^23 + q with one byte permute
+    // (bytes q, 0, 0, 0x4B), minus 2^23 exactly
+    const uint32_t nib = (w[i] >> sh) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float qf = __uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7540u | e)) - 8388608.f;
+      o[4 * i + e] = __fsub_rn(__fmul_rn(dsc, qf), dm);
+    }
   }
 }
 
