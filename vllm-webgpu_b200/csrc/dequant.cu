@@ -40,11 +40,9 @@ __device__ __forceinline__ void ldg_words_a2(const uint8_t* p, uint32_t* w) {
   for (int i = 0; i < NW; ++i) w[i] = __funnelshift_r(t[i], t[i + 1], 16);
 }
 
-// Exact float of a small integer (|v| < 2^22) without the quarter-rate int->float
-// conversion: 1.5*2^23 + v has v in its low mantissa bits; one add removes the offset.
-__device__ __forceinline__ float small_int_to_float(int v) {
-  return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.f);
-}
+// Quants become exact floats without the quarter-rate int->float conversion: a
+// byte permute builds the float 2^23 + u from a byte u (bytes u, 0, 0, 0x4B), and
+// one subtraction removes the offset (and the format's bias) exactly.
 
 __device__ __forceinline__ uint32_t byte_of(const uint32_t* w, int i) { return (w[i >> 2] >> (8 * (i & 3))) & 0xFFu; }
 
@@ -59,10 +57,14 @@ __device__ __forceinline__ void dequant32<kQ4_0>(const uint8_t* row, int unit, f
   uint32_t w[4];
   ldg_words_a2<4>(b + 2, w);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    uint32_t v = byte_of(w, j);
-    o[j] = __fmul_rn(d, small_int_to_float(static_cast<int>(v & 15u) - 8));
-    o[j + 16] = __fmul_rn(d, small_int_to_float(static_cast<int>(v >> 4) - 8));
+  for (int i = 0; i < 4; ++i) {
+    // bytes q, 0, 0, 0x4B = the float 2^23 + q; minus 2^23 + 8 gives q - 8 exactly
+    const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[4 * i + e] = __fmul_rn(d, __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u | e)) - 8388616.f);
+      o[16 + 4 * i + e] = __fmul_rn(d, __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u | e)) - 8388616.f);
+    }
   }
 }
 
@@ -74,9 +76,12 @@ __device__ __forceinline__ void dequant32<kQ8_0>(const uint8_t* row, int unit, f
   uint32_t w[8];
   ldg_words_a2<8>(b + 2, w);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    int q = static_cast<int>(static_cast<int8_t>(byte_of(w, j)));
-    o[j] = __fmul_rn(small_int_to_float(q), d);
+  for (int i = 0; i < 8; ++i) {
+    // q ^ 0x80 = q + 128 as an unsigned byte: float 2^23 + q + 128, minus 2^23 + 128
+    const uint32_t u = w[i] ^ 0x80808080u;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o[4 * i + e] = __fmul_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540u | e)) - 8388736.f, d);
   }
 }
 
@@ -136,9 +141,12 @@ __device__ __forceinline__ void dequant32<kQ6_K>(const uint8_t* row, int unit, f
   const float dl1 = __fmul_rn(d, static_cast<float>(static_cast<int8_t>(scw >> 8)));
   const int shl = 4 * (u >> 1), shh = 2 * u;
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    int q = static_cast<int>(((byte_of(ql, c) >> shl) & 15u) | (((byte_of(qh, c) >> shh) & 3u) << 4)) - 32;
-    o[c] = __fmul_rn(c < 16 ? dl0 : dl1, small_int_to_float(q));
+  for (int i = 0; i < 8; ++i) {
+    // four 6-bit quants per word: low nibble | 2 high bits << 4; float 2^23 + q6, minus 2^23 + 32
+    const uint32_t q6 = ((ql[i] >> shl) & 0x0F0F0F0Fu) | (((qh[i] >> shh) & 0x03030303u) << 4);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o[4 * i + e] = __fmul_rn(i < 4 ? dl0 : dl1, __uint_as_float(__byte_perm(q6, 0x4B000000u, 0x7540u | e)) - 8388640.f);
   }
 }
 
