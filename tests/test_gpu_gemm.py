@@ -58,6 +58,24 @@ def test_gemm_many_tiles_per_cta_ragged(cuda, qt):
     assert _check(qt, 1100, 20000, 512, rows=512) <= TOL
 
 
+@pytest.mark.parametrize("xd", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("m", [100, 300])
+def test_gemm_strided_unaligned_x(cuda, xd, m):
+    """Activations as a column slice of a wider buffer (base off 16-byte alignment,
+    odd row stride) take the element-wise cast; aligned ones the vector cast."""
+    from vllm_webgpu_b200 import ops
+    qt, n, k = O.Q4_K, 512, 1024
+    raw = O.make_weights(n, k, qt, seed=3)
+    xs = torch.from_numpy(O.make_activations(m, k, seed=4)).to(xd)
+    wide = torch.zeros((m, k + 3), dtype=xd)
+    wide[:, 1:k + 1] = xs
+    x = wide.cuda()[:, 1:k + 1]
+    y = ops.gemm(x, _wt(raw, qt, n, k), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref = O.matmul_ref(xs.float().numpy(), raw, qt, n, k)
+    assert O.rel_err(y.cpu().numpy(), ref) <= TOL
+
+
 def test_gemm_prefill_8192_sampled(cuda):
     assert _check(O.Q4_K, 8192, 14336, 4096, rows=128) <= TOL
 

@@ -228,8 +228,9 @@ cudaError_t launch_dequant(const void* q, int qtype, int64_t n_rows, int64_t k, 
 // Activation cast x[M, K] (row stride ldx, f32/f16/bf16) -> fp16 [M, K]
 // contiguous, 8 elements per thread. bf16 -> fp16 is exact for |x| in the
 // fp16 normal range; values beyond +-65504 become +-inf.
+// Any alignment: element loads.
 template <int XT>
-__global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict__ x, int64_t m, int64_t k,
+__global__ void __launch_bounds__(256) cast_x_f16_scalar_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                                          int64_t ldx, __half* __restrict__ out) {
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const int64_t total = m * k;
@@ -252,14 +253,59 @@ __global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict_
   *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<uint4*>(tmp);
 }
 
+// 16-byte aligned rows: vector loads (fp16 input is a plain copy).
+template <int XT>
+__global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict__ x, int64_t m, int64_t k,
+                                                         int64_t ldx, __half* __restrict__ out) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  const int64_t total = m * k;
+  if (i >= total) return;
+  const int64_t r = i / k, c = i - r * k;
+  // k is a multiple of 32, so c..c+7 never straddles a row and out+i is 16-byte aligned;
+  // the caller guarantees 16-byte aligned input rows (row stride and base)
+  float v[8];
+  if (XT == GGUFMM_F32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + r * ldx + c);
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 p = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + r * ldx + c);
+    if (XT == GGUFMM_F16) {
+      *reinterpret_cast<uint4*>(out + i) = p;
+      return;
+    }
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+  uint32_t h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    __half2 h2 = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    h[j] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  *reinterpret_cast<uint4*>(out + i) = make_uint4(h[0], h[1], h[2], h[3]);
+}
+
 cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, void* out,
                               cudaStream_t st) {
   const int64_t n8 = (m * k + 7) / 8;
   const unsigned blocks = static_cast<unsigned>((n8 + 255) / 256);
   __half* o = static_cast<__half*>(out);
-  if (x_dtype == GGUFMM_F32) cast_x_f16_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-  else if (x_dtype == GGUFMM_F16) cast_x_f16_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-  else cast_x_f16_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  const int es = x_dtype == GGUFMM_F32 ? 4 : 2;
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * es) % 16 == 0;
+  if (vec) {
+    if (x_dtype == GGUFMM_F32) cast_x_f16_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+    else if (x_dtype == GGUFMM_F16) cast_x_f16_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+    else cast_x_f16_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  } else {
+    if (x_dtype == GGUFMM_F32) cast_x_f16_scalar_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+    else if (x_dtype == GGUFMM_F16) cast_x_f16_scalar_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+    else cast_x_f16_scalar_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
+  }
   return cudaGetLastError();
 }
 
