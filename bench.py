@@ -353,7 +353,7 @@ def run_ours(args, rank: int, world: int) -> None:
         tf = 2.0 * pm * pn * pk / (pms / 1e3) / 1e12
         pre = {"workload": "q4k_prefill_m2048_k4096_n14336", "ms": round(pms, 4), "tflops": round(tf, 2),
                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
-               "path": "dequant->fp16 workspace + tcgen05 GEMM (2 kernels)"}
+               "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
