@@ -460,10 +460,12 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
         const float s = live ? __uint_as_float((E - 21u) << 23) : 0.f;
         // Balanced digits in one add: Y = X + 0x808080 (>= 0 as |X| <= 2^22) has the
         // bytes d3 + 128, d2 + 128, d1 + 128, so Y ^ 0x808080 holds d3, d2, d1 as s8.
+        // rint(x * inv) without a float->int conversion: x * inv + 1.5 * 2^23 stays in
+        // [2^23, 2^24), so its bit pattern is 0x4B400000 + X (rounded to nearest even)
         uint32_t z[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          z[i] = (static_cast<uint32_t>(__float2int_rn(v[bt][i] * inv)) + 0x808080u) ^ 0x808080u;
+          z[i] = (__float_as_uint(fmaf(v[bt][i], inv, 12582912.f)) + (0x808080u - 0x4B400000u)) ^ 0x808080u;
         uint32_t dg[3][2];  // [digit][word]: 8 digit bytes of this lane (digit 0 = d1, the top byte)
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
