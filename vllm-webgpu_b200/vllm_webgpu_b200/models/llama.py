@@ -76,3 +76,27 @@ class LlamaB200Model(BaseB200Model):
         self.project_gate_up(layer, ffn_normed, bufs["gate"], bufs["up"])
         self.project_down(layer, ffn_act, bufs["down"])
         return bufs
+
+    def layer_linears_graph(self, layer: int, normed, attn_out, ffn_normed, ffn_act, bufs: dict) -> dict:
+        """``layer_linears`` replayed from a CUDA graph, the decode serving path:
+        the launches are captured once per (layer, buffer addresses) and then
+        replayed with one host call. The inputs and ``bufs`` must be the same
+        tensors (static buffers the caller refills) on every call; the replay is
+        ordered on the current stream."""
+        key = (layer, normed.data_ptr(), attn_out.data_ptr(), ffn_normed.data_ptr(), ffn_act.data_ptr(),
+               tuple((k, b.data_ptr()) for k, b in sorted(bufs.items())))
+        graphs = self.__dict__.setdefault("_layer_graphs", {})
+        g = graphs.get(key)
+        cur = torch.cuda.current_stream(self.device)
+        if g is None:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)  # warm-up
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)
+            cur.wait_stream(side)
+            graphs[key] = g
+        g.replay()
+        return bufs
