@@ -190,13 +190,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
         const int shn = hi ? 4 : 0;
         const float ds = hi ? dsc_hi : dsc_lo, nd = hi ? ndm_hi : ndm_lo;
         uint32_t out[4];
+        // four nibbles per mask; each becomes the float 2^23 + q with one byte permute
+        const uint32_t na = (wa >> shn) & 0x0F0F0F0Fu, nb = (wb >> shn) & 0x0F0F0F0Fu;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const uint32_t src = e < 2 ? wa : wb;
-          const int b0 = (2 * e) & 3;
-          const float v0 = fmaf(ds, small_uint_to_float((src >> (8 * b0 + shn)) & 15u), nd);
-          const float v1 = fmaf(ds, small_uint_to_float((src >> (8 * (b0 + 1) + shn)) & 15u), nd);
-          __half2 h2 = __floats2half2_rn(v0, v1);
+          const uint32_t src = e < 2 ? na : nb;
+          const uint32_t b0 = (2u * e) & 3u;
+          const float q0 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | b0)) - 8388608.f;
+          const float q1 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1))) - 8388608.f;
+          __half2 h2 = __floats2half2_rn(fmaf(ds, q0, nd), fmaf(ds, q1, nd));
           out[e] = *reinterpret_cast<uint32_t*>(&h2);
         }
         *reinterpret_cast<uint4*>(arow + ((kc ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
