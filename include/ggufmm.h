@@ -127,6 +127,21 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
                         void* const* y, int y_dtype, const int64_t* ldy, void* stream);
 
 /*
+ * Fused SwiGLU decode GEMV: y[m, n] = silu(sum_k x[m, k] Wg[n, k]) * (sum_k x[m, k] Wu[n, k])
+ * for 1 <= M <= 8, the gate and up weights (same qtype, N and K) streamed by one
+ * launch and combined in its epilogue (silu(g) = g / (1 + exp(-g)), fp32). It
+ * replaces the reference's gate and up dispatches (vllm_webgpu/models/llama.py:343-348)
+ * plus its SwiGLU shader (shaders/generic/gelu_mul.wgsl:14-20: silu(gate) * up in
+ * fp32, dispatched at llama.py:350-352), which the reference runs as three passes. Q4_K and Q4_0 with K a multiple of
+ * 256 only (GGUFMM_ERR_QTYPE / GGUFMM_ERR_SHAPE otherwise, nothing launched);
+ * the other requirements are those of ggufmm_gemv. Tolerance: the gate and up
+ * sums are those of ggufmm_gemv; the product is formed in fp32.
+ */
+int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k,
+                       const void* x, int x_dtype, int64_t m, int64_t ldx,
+                       void* y, int y_dtype, int64_t ldy, void* stream);
+
+/*
  * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
  * arguments). Size it once for the largest M and reuse it.
  */

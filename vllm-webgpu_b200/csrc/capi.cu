@@ -35,7 +35,7 @@ cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_i8_supported(int qtype, int64_t k, int m);
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
-                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st);
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu = 0);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                             int64_t ldy, cudaStream_t st);
 
@@ -217,6 +217,30 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
     if (s) return s;
   }
   return GGUFMM_OK;
+}
+
+int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k, const void* x,
+                       int x_dtype, int64_t m, int64_t ldx, void* y, int y_dtype, int64_t ldy, void* stream) {
+  int s = check_matmul_args(q_gate, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (!q_up) return GGUFMM_ERR_ARG;
+  if (m > 8) return GGUFMM_ERR_SHAPE;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  if (!aligned(q_gate, 16) || !aligned(q_up, 16) || row_bytes % 16 || !aligned(x, 16) ||
+      (ldx * elem_size(x_dtype)) % 16 || !aligned(y, elem_size(y_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  s = check_device();
+  if (s) return s;
+  // the fused epilogue lives in the integer tensor-core GEMV (Q4_K, Q4_0, K a multiple of 256)
+  if (!gemv_i8_supported(qtype, k, static_cast<int>(m))) return qtype == GGUFMM_Q4_K || qtype == GGUFMM_Q4_0
+                                                                    ? GGUFMM_ERR_SHAPE
+                                                                    : GGUFMM_ERR_QTYPE;
+  const void* qs[2] = {q_gate, q_up};
+  const int64_t ns[2] = {n, n};
+  void* ys[2] = {y, y};
+  const int64_t lds[2] = {ldy, ldy};
+  return cuda_status(launch_gemv_i8_grouped(2, qs, ns, qtype, k, x, x_dtype, m, ldx, ys, y_dtype, lds, row_bytes,
+                                            static_cast<cudaStream_t>(stream), 1));
 }
 
 static size_t round256(size_t v) { return (v + 255) / 256 * 256; }

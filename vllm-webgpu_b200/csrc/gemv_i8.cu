@@ -85,6 +85,7 @@ struct I8Args {
   int xd_pitch;      // bytes per digit column of x
   int red_stride;    // floats per warp in one reduction buffer
   int ksplit;        // 1, or 2: K halves on the two CTAs of a cluster, partials joined in rank 0
+  int swiglu;        // segments 0 (gate) and 1 (up) of equal N: y = silu(gate) * up into segment 0's y
   uint32_t xd_off;   // int8 digits [3m cols][k]
   uint32_t xf_off;   // float fold factors [unit][8 NCG cols]: s * radix
   uint32_t xs_off;   // Q4_K: bf16 x sums [unit][8 NCC cols][8 sub-blocks]; Q4_0: int -8*digit sums [block][8 NCG cols]
@@ -315,6 +316,23 @@ __device__ __forceinline__ const Seg& seg_of(const I8Args& a, int64_t rb) {
   return a.seg[i];
 }
 
+// The j-th row block of cluster / CTA `cid`: plain, every ncl-th block; SwiGLU,
+// every ncl-th PAIR of blocks (gate rows, then the same up rows), so the epilogue
+// holds the gate sums when the up sums arrive.
+__device__ __forceinline__ int64_t block_of(const I8Args& a, int64_t cid, int64_t ncl, int64_t j) {
+  return a.swiglu ? 2 * (cid + (j >> 1) * ncl) + (j & 1) : cid + j * ncl;
+}
+// Segment and first weight row of logical row block lb.
+__device__ __forceinline__ const Seg& block_rows(const I8Args& a, int64_t lb, int64_t& r0) {
+  if (a.swiglu) {
+    r0 = (lb >> 1) * kRows;
+    return a.seg[lb & 1];
+  }
+  const Seg& sg = seg_of(a, lb);
+  r0 = (lb - sg.rb0) * kRows;
+  return sg;
+}
+
 // Position of element e (0..31) of a Q4_0 block inside its 32 permuted digit
 // bytes: thread t's MMA k 4t..4t+3 (elements 4t..) and 16+4t.. (elements 16+4t..)
 // become bytes 8t..8t+7.
@@ -334,7 +352,8 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   // with the K split, the two CTAs of a cluster (consecutive blockIdx.x) share row blocks
   const int rank = a.ksplit == 2 ? static_cast<int>(blockIdx.x & 1) : 0;
   const int64_t cid = blockIdx.x / a.ksplit, ncl = gridDim.x / a.ksplit;
-  const int64_t my_blocks = a.nrowblocks > cid ? (a.nrowblocks - 1 - cid) / ncl + 1 : 0;
+  const int64_t nunits = a.swiglu ? a.nrowblocks / 2 : a.nrowblocks;  // blocks, or gate/up pairs
+  const int64_t my_blocks = (nunits > cid ? (nunits - 1 - cid) / ncl + 1 : 0) * (a.swiglu ? 2 : 1);
   const int64_t total_pieces = my_blocks * a.nchunks;
   const int units = a.k / kUnitK / a.ksplit;  // this CTA's units along K
   const int ku0 = rank * units;                // ... starting here
@@ -358,10 +377,10 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   }
 
   auto issue = [&](int64_t p, int s) {
-    const int64_t rb = cid + (p / a.nchunks) * ncl;
+    const int64_t rb = block_of(a, cid, ncl, p / a.nchunks);
     const int ch = static_cast<int>(p % a.nchunks);
-    const Seg& sg = seg_of(a, rb);
-    const int64_t r0 = (rb - sg.rb0) * kRows;
+    int64_t r0;
+    const Seg& sg = block_rows(a, rb, r0);
     const int nr = static_cast<int>((sg.n - r0) < kRows ? (sg.n - r0) : kRows);
     const int nu = min(a.chunk_units, units - ch * a.chunk_units);
     const uint32_t bytes = static_cast<uint32_t>(nu * a.unit_bytes);
@@ -536,18 +555,25 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
 
     if (warp == W + 1) {
       // ---------------- epilogue ----------------
+      float gv[8];  // SwiGLU: this lane's gate sums of the current pair (one per token pass)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gv[i] = 0.f;
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
         const int b = static_cast<int>(blk & 1);
         if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
-        const int64_t rb = cid + blk * ncl;
+        const int64_t rb = block_of(a, cid, ncl, blk);
         const float* rbuf = red + b * (W * a.red_stride);
-        const Seg& sg = seg_of(a, rb);
+        int64_t r0;
+        const Seg& sg = block_rows(a, rb, r0);
         float* xslot = reinterpret_cast<float*>(smem + a.xchg_off) + b * (8 * kRows);
         if (rank == 1 && blk >= 2 && !mbar_wait_cluster(&xempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
         if (rank == 0 && a.ksplit == 2 && !mbar_wait_cluster(&xfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
         // lane = (row, half): rows on consecutive lanes read consecutive words of
         // the column-major partials (no bank conflicts); each half sums W/2 warps
-        for (int i = lane; i < 32 * a.m; i += 32) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          if (it >= a.m) break;
+          const int i = lane + 32 * it;
           const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
           float v = 0.f;
 #pragma unroll
@@ -557,13 +583,22 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
             if (QT == kQ4_K) v -= rw[kRows * kDCols + tok * kRows + row];
           }
           v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
-          const int64_t n_idx = (rb - sg.rb0) * kRows + phys_row(row, a.rg);
+          const int64_t n_idx = r0 + phys_row(row, a.rg);
           if (rank == 1) {
             // this CTA's K half goes to rank 0, which adds it and stores y
             if (half == 0) st_cluster_f32(cluster_addr(xslot + tok * kRows + row, 0), v);
           } else {
             if (a.ksplit == 2) v += xslot[tok * kRows + row];
-            if (half == 0 && n_idx < sg.n) store_y_rt(sg.y, a.ytype, tok * sg.ldy + n_idx, v);
+            if (a.swiglu) {
+              if ((blk & 1) == 0) {
+                gv[it] = v;  // gate: kept until the up rows of the pair
+                continue;
+              }
+              const float g = gv[it];
+              v = g / (1.f + __expf(-g)) * v;  // silu(gate) * up
+            }
+            const Seg& so = a.swiglu ? a.seg[0] : sg;
+            if (half == 0 && n_idx < so.n) store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
           }
         }
         if (rank == 1) {
@@ -825,10 +860,12 @@ bool gemv_i8_supported(int qtype, int64_t k, int m) {
 
 // nseg weights of one qtype and K (16-byte aligned bases, row bytes a multiple
 // of 16) against the same activations, one launch.
+// swiglu: nseg = 2 (gate, up) of equal N; y[0] receives silu(x Wg^T) * (x Wu^T).
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
-                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st) {
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu) {
   if (nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+  if (swiglu && (nseg != 2 || n[0] != n[1])) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -848,6 +885,7 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
     rb += (n[i] + kRows - 1) / kRows;
   }
   a.nrowblocks = rb;
+  a.swiglu = swiglu;
   a.k = static_cast<int>(k);
   a.row_bytes = row_bytes;
   a.x = x;

@@ -68,6 +68,30 @@ class LlamaB200Model(BaseB200Model):
     def project_down(self, layer: int, ffn_act: torch.Tensor, out: torch.Tensor):
         return self._linear(ffn_act, self._w(layer, "down"), out)
 
+    def project_ffn_act(self, layer: int, ffn_normed: torch.Tensor, act_buf: torch.Tensor) -> torch.Tensor:
+        """The FFN activation silu(gate) * up into ``act_buf``: in decode one fused
+        launch (ggufmm_gemv_swiglu), where the reference runs the gate and up
+        dispatches and its gelu_mul SwiGLU shader (llama.py:343-352); otherwise the
+        two projections and the activation separately."""
+        gate, up = self._w(layer, "gate"), self._w(layer, "up")
+        if (isinstance(gate, GGUFQuantTensor) and isinstance(up, GGUFQuantTensor)
+                and ops.swiglu_fusable(ffn_normed, gate, up)):
+            try:
+                return ops.gemv_swiglu(ffn_normed, gate, up, out=act_buf.reshape(-1, gate.n))
+            except ValueError:
+                pass  # activations too large for the fused kernel's shared memory
+        g = torch.empty_like(act_buf, dtype=torch.float32)
+        u = torch.empty_like(act_buf, dtype=torch.float32)
+        self.project_gate_up(layer, ffn_normed, g, u)
+        act_buf.copy_(torch.nn.functional.silu(g) * u)
+        return act_buf
+
+    def project_lm_head(self, hidden: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+        """Logits from the final hidden state on the GGUF output weight (``lm_head.weight``,
+        GGUF ``output.weight``), quantized like the other projections (the reference
+        forces an f16 head, llama.py:228-235)."""
+        return self._linear(hidden, self.weights["lm_head.weight"], logits)
+
     def layer_linears(self, layer: int, normed, attn_out, ffn_normed, ffn_act, bufs: dict) -> dict:
         """All seven projections of one layer into caller-owned ``bufs``
         (keys q, k, v, o, gate, up, down)."""

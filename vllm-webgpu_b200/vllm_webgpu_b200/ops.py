@@ -118,6 +118,30 @@ def gemv_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Te
     return ys
 
 
+def swiglu_fusable(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor) -> bool:
+    """Whether gemv_swiglu handles these operands (decode M, Q4_K / Q4_0, K % 256 == 0)."""
+    m = x.numel() // max(x.shape[-1], 1)
+    return (1 <= m <= GEMV_MAX_M and gate.qtype == up.qtype and gate.qtype in (2, 12) and gate.shape == up.shape
+            and gate.k % 256 == 0 and x.shape[-1] == gate.k)
+
+
+def gemv_swiglu(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Fused FFN input for decode (M <= 8): out = silu(x gate^T) * (x up^T), one launch
+    (the gate and up GEMVs and the SwiGLU of the reference's three dispatches)."""
+    if gate.shape != up.shape or gate.qtype != up.qtype:
+        raise ValueError("gate and up must share shape and quantization type")
+    dev = _require_cuda(x, gate.data, up.data)
+    x2 = _as_2d(x, gate.k)
+    y = _out(x2, gate.n, out, out_dtype)
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemv_swiglu(gate.data.data_ptr(), up.data.data_ptr(), gate.qtype, gate.n, gate.k,
+                                           x2.data_ptr(), _code(x2.dtype), x2.shape[0], x2.stride(0),
+                                           y.data_ptr(), _code(y.dtype), y.stride(0), _stream(dev))
+    _lib.check(st, "ggufmm_gemv_swiglu")
+    return y
+
+
 _workspaces: dict[int, torch.Tensor] = {}
 
 

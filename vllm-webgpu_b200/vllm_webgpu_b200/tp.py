@@ -59,6 +59,8 @@ class TensorParallelSwiGLU:
         else:
             self.gate, self.up, self.down = shard_ffn(gate, up, down, rank, world)
         self.rank, self.world, self.group = rank, world, group
+        # the fused gate/up/SwiGLU GEMV serves decode unless a custom matmul is injected
+        self.fused_swiglu = matmul is None
         if matmul is None:
             from .ops import mul_mat
             matmul = mul_mat
@@ -66,9 +68,20 @@ class TensorParallelSwiGLU:
         self.reduce_dtype = reduce_dtype
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        g = self.matmul(x, self.gate, out_dtype=torch.float32)
-        u = self.matmul(x, self.up, out_dtype=torch.float32)
-        act = torch.nn.functional.silu(g) * u  # fp32 SwiGLU, fed to down in fp32
+        act = None
+        if self.fused_swiglu and x.is_cuda:
+            from . import ops
+            if ops.swiglu_fusable(x, self.gate, self.up):
+                # decode: gate, up and SwiGLU in one launch (fp32 activation); shapes whose
+                # activations do not fit the kernel's shared memory take the unfused path
+                try:
+                    act = ops.gemv_swiglu(x, self.gate, self.up, out_dtype=torch.float32)
+                except ValueError:
+                    act = None
+        if act is None:
+            g = self.matmul(x, self.gate, out_dtype=torch.float32)
+            u = self.matmul(x, self.up, out_dtype=torch.float32)
+            act = torch.nn.functional.silu(g) * u  # fp32 SwiGLU, fed to down in fp32
         y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
         if self.world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
