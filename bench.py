@@ -368,6 +368,40 @@ def run_ours(args, rank: int, world: int) -> None:
                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
                "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
 
+    # tensor-parallel SwiGLU FFN (config 5): Llama-3-70B shape, Q4_K, intermediate split over
+    # the ranks, one NCCL all-reduce per step (decode M=1 and M=32); eager, host-issued steps
+    tpf = None
+    if not args.no_tp:
+        from vllm_webgpu_b200.tp import TensorParallelSwiGLU
+        hid, inter = 8192, 28672
+        full = [random_weights(inter, hid, Q4_K, seed=901, device=dev), random_weights(inter, hid, Q4_K, seed=902, device=dev),
+                random_weights(hid, inter, Q4_K, seed=903, device=dev)]
+        ffn = TensorParallelSwiGLU(*full, rank=rank, world=world)
+        del full
+        wbytes = 3 * hid * inter // 256 * 144
+        tpf = {"workload": "q4k_llama3_70b_ffn_tp", "tp": world, "weight_bytes_total": wbytes,
+               "path": "fused gate/up/SwiGLU GEMV (M<=8) or GEMMs, down projection, NCCL all-reduce"}
+        for mt in (1, 32):
+            xt = torch.randn((mt, hid), generator=g, device=dev).to(torch.bfloat16)
+            for _ in range(3):
+                ffn(xt)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            it = 50
+            e0.record(stream)
+            for _ in range(it):
+                ffn(xt)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            tms = e0.elapsed_time(e1) / it
+            if world > 1:
+                t = torch.tensor([tms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                tms = float(t.item())
+            tpf[f"m{mt}"] = {"us_per_step": round(tms * 1e3, 2), "weight_gbs": round(wbytes / (tms / 1e3) / 1e9, 2)}
+        del ffn
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_rate(args.cpu_seconds)
@@ -394,6 +428,7 @@ def run_ours(args, rank: int, world: int) -> None:
             "gpu_launches": len(GROUPS) * steps,
             "clocks": clocks,
             "prefill": pre,
+            "tp_ffn": tpf,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -407,6 +442,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
