@@ -142,6 +142,33 @@ int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t 
                        void* y, int y_dtype, int64_t ldy, void* stream);
 
 /*
+ * Decode GEMV whose result is all-reduced (summed) over `world` GPUs in the same
+ * kernel, through NVLink peer memory: the tensor-parallel FFN's down projection
+ * (each GPU holds a column slice of W over its share of the intermediate
+ * dimension), replacing the GEMV followed by a separate NCCL all-reduce. Every
+ * GPU of the group makes this call with the same shapes and `epoch`; each writes
+ * its fp32 partial of every 16-row block into every GPU's exchange buffer over
+ * NVLink, publishes a per-block flag (release, system scope), waits (bounded) for
+ * the other GPUs' flags and stores the sum of the partials in rank order, so all
+ * GPUs hold bit-identical y[m, n].
+ *   peer_bufs  the `world` exchange buffers (device pointers valid on this GPU,
+ *              e.g. from CUDA IPC / symmetric memory; 256-byte aligned), each
+ *              ggufmm_gemv_allreduce_buffer_bytes(n, m_max, world) bytes and
+ *              zero-filled before the first call
+ *   epoch      1 for the first call on these buffers, +1 on every later call
+ *              (partials alternate between two halves by epoch parity)
+ * Q4_K / Q4_0, 1 <= M <= m_max <= 8, 2 <= world <= 8; otherwise as ggufmm_gemv.
+ * A GPU whose peers never make the matching call gives up after a bounded wait
+ * (ggufmm_device_status reports it). The reference has no multi-GPU path.
+ */
+size_t ggufmm_gemv_allreduce_buffer_bytes(int64_t n, int64_t m_max, int world);
+int ggufmm_gemv_allreduce(const void* q, int qtype, int64_t n, int64_t k,
+                          const void* x, int x_dtype, int64_t m, int64_t ldx,
+                          void* y, int y_dtype, int64_t ldy,
+                          void* const* peer_bufs, int world, int rank, int64_t m_max,
+                          uint32_t epoch, void* stream);
+
+/*
  * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
  * arguments). Size it once for the largest M and reuse it.
  */

@@ -78,7 +78,7 @@ def test_tp_ffn_two_gpus_nccl(cuda, tmp_path):
     script = tmp_path / "worker.py"
     script.write_text(WORKER.format(root=ROOT))
     out = tmp_path / "y.npy"
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", GGUFMM_TP_FUSED="0")  # the NCCL all-reduce path
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
                         "--master-addr", "127.0.0.1", "--master-port", "29533", str(script), str(out)],
                        env=env, capture_output=True, text=True, timeout=600, cwd=ROOT)
@@ -86,3 +86,49 @@ def test_tp_ffn_two_gpus_nccl(cuda, tmp_path):
     x = O.make_activations(8, H, seed=4)
     xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     assert O.rel_err(np.load(out), _oracle_ffn(xb)) <= TOL
+
+
+WORKER_FUSED = r"""
+import os, sys, numpy as np, torch, torch.distributed as dist
+sys.path.insert(0, {root!r}); sys.path.insert(0, os.path.join({root!r}, "vllm-webgpu_b200"))
+from tests.test_gpu_tp import _ffn, H
+from oracle import gguf_oracle as O
+from vllm_webgpu_b200 import _lib
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+ffn = _ffn(rank, world)
+outs = []
+for m, seed in ((1, 5), (8, 6), (1, 7)):  # three calls: both halves of the exchange buffers
+    x = O.make_activations(m, H, seed=seed)
+    y = ffn(torch.from_numpy(x).to(torch.bfloat16).cuda())
+    torch.cuda.synchronize()
+    outs.append(y.cpu().numpy())
+assert ffn._exchange is not None, "the fused down-projection all-reduce did not run"
+assert _lib.lib().ggufmm_device_status(1, None) == 0
+np.savez(sys.argv[1] + f".{{rank}}.npz", *outs)
+dist.destroy_process_group()
+"""
+
+
+def test_tp_ffn_two_gpus_fused_allreduce(cuda, tmp_path):
+    """Decode TP FFN on 2 GPUs whose down projection and all-reduce are one kernel
+    (partials exchanged through NVLink peer memory): both GPUs hold the same bits,
+    equal to the oracle FFN within the matmul gate."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "worker_fused.py"
+    script.write_text(WORKER_FUSED.format(root=ROOT))
+    out = tmp_path / "y"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", "29534", str(script), str(out)],
+                       env=env, capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-3000:]
+    y0, y1 = np.load(str(out) + ".0.npz"), np.load(str(out) + ".1.npz")
+    for i, (m, seed) in enumerate(((1, 5), (8, 6), (1, 7))):
+        a, b = y0[f"arr_{i}"], y1[f"arr_{i}"]
+        assert np.array_equal(a, b)
+        x = O.make_activations(m, H, seed=seed)
+        xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+        assert O.rel_err(a, _oracle_ffn(xb)) <= TOL

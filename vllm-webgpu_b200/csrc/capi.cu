@@ -35,7 +35,15 @@ cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_i8_supported(int qtype, int64_t k, int m);
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
-                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu = 0);
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu,
+                                   const struct GemvTp* tp);
+struct GemvTp {
+  int world, rank;
+  uint32_t epoch;
+  int64_t m_max;
+  const void* const* bufs;
+};
+size_t gemv_tp_buffer_bytes(int64_t n, int64_t m_max, int world);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                             int64_t ldy, cudaStream_t st);
 
@@ -183,7 +191,7 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   // CUDA-core streaming GEMV
   if (gemv_i8_supported(qtype, k, static_cast<int>(m)))
     return cuda_status(launch_gemv_i8_grouped(1, &q, &n, qtype, k, x, x_dtype, m, ldx, &y, y_dtype, &ldy, row_bytes,
-                                              static_cast<cudaStream_t>(stream)));
+                                              static_cast<cudaStream_t>(stream), 0, nullptr));
   if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype))
     return cuda_status(launch_gemv_mma(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                        static_cast<cudaStream_t>(stream)));
@@ -208,7 +216,7 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
   if (s) return s;
   if (one_launch && gemv_i8_supported(qtype, k, static_cast<int>(m)))
     return cuda_status(launch_gemv_i8_grouped(nseg, q, n, qtype, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
-                                              static_cast<cudaStream_t>(stream)));
+                                              static_cast<cudaStream_t>(stream), 0, nullptr));
   if (one_launch && gemv_mma_supported(qtype, n[0], k, static_cast<int>(m), x_dtype))
     return cuda_status(launch_gemv_mma_grouped(nseg, q, n, qtype, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
                                                static_cast<cudaStream_t>(stream)));
@@ -240,7 +248,35 @@ int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t 
   void* ys[2] = {y, y};
   const int64_t lds[2] = {ldy, ldy};
   return cuda_status(launch_gemv_i8_grouped(2, qs, ns, qtype, k, x, x_dtype, m, ldx, ys, y_dtype, lds, row_bytes,
-                                            static_cast<cudaStream_t>(stream), 1));
+                                            static_cast<cudaStream_t>(stream), 1, nullptr));
+}
+
+size_t ggufmm_gemv_allreduce_buffer_bytes(int64_t n, int64_t m_max, int world) {
+  if (n <= 0 || m_max < 1 || m_max > 8 || world < 2 || world > 8) return 0;
+  return gemv_tp_buffer_bytes(n, m_max, world);
+}
+
+int ggufmm_gemv_allreduce(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                          int64_t ldx, void* y, int y_dtype, int64_t ldy, void* const* peer_bufs, int world,
+                          int rank, int64_t m_max, uint32_t epoch, void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (!peer_bufs) return GGUFMM_ERR_ARG;
+  if (world < 2 || world > 8 || rank < 0 || rank >= world || m > m_max || m_max > 8 || epoch == 0)
+    return GGUFMM_ERR_ARG;
+  for (int i = 0; i < world; ++i)
+    if (!peer_bufs[i] || !aligned(peer_bufs[i], 256)) return GGUFMM_ERR_ALIGN;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  if (!aligned(q, 16) || row_bytes % 16 || !aligned(x, 16) || (ldx * elem_size(x_dtype)) % 16 ||
+      !aligned(y, elem_size(y_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  s = check_device();
+  if (s) return s;
+  if (!gemv_i8_supported(qtype, k, static_cast<int>(m)))
+    return qtype == GGUFMM_Q4_K || qtype == GGUFMM_Q4_0 ? GGUFMM_ERR_SHAPE : GGUFMM_ERR_QTYPE;
+  const GemvTp tp{world, rank, epoch, m_max, peer_bufs};
+  return cuda_status(launch_gemv_i8_grouped(1, &q, &n, qtype, k, x, x_dtype, m, ldx, &y, y_dtype, &ldy, row_bytes,
+                                            static_cast<cudaStream_t>(stream), 0, &tp));
 }
 
 static size_t round256(size_t v) { return (v + 255) / 256 * 256; }

@@ -86,6 +86,13 @@ struct I8Args {
   int red_stride;    // floats per warp in one reduction buffer
   int ksplit;        // 1, or 2: K halves on the two CTAs of a cluster, partials joined in rank 0
   int swiglu;        // segments 0 (gate) and 1 (up) of equal N: y = silu(gate) * up into segment 0's y
+  // all-reduce over tp_world GPUs through peer memory (tp_world > 1): every GPU's
+  // exchange buffer, [2 parities][tp_world sources][m_max][n] fp32 partials then
+  // [2][tp_world][row blocks] u32 flags; y = the sum of the partials
+  int tp_world, tp_rank;
+  uint32_t epoch;
+  int64_t m_max, tp_nrb, tp_flag_off;  // flag_off in bytes
+  uint64_t peer[8];
   uint32_t xd_off;   // int8 digits [3m cols][k]
   uint32_t xf_off;   // float fold factors [unit][8 NCG cols]: s * radix
   uint32_t xs_off;   // Q4_K: bf16 x sums [unit][8 NCC cols][8 sub-blocks]; Q4_0: int -8*digit sums [block][8 NCG cols]
@@ -122,6 +129,25 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   atomicOr(&g_device_error, kErrWaitTimeout);
   return false;
 }
+// ---- peer-memory (NVLink) exchange for the fused all-reduce ----
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// bounded: gives up (error word) rather than hang when a peer never publishes
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t want) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (ld_acquire_sys(p) == want) return true;
+    if (i > 64) __nanosleep(128);
+  }
+  atomicOr(&g_device_error, kErrWaitTimeout);
+  return false;
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -556,6 +582,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     if (warp == W + 1) {
       // ---------------- epilogue ----------------
       float gv[8];  // SwiGLU: this lane's gate sums of the current pair (one per token pass)
+      float pv[8];  // all-reduce: this lane's partials of the current row block
 #pragma unroll
       for (int i = 0; i < 8; ++i) gv[i] = 0.f;
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
@@ -598,7 +625,55 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
               v = g / (1.f + __expf(-g)) * v;  // silu(gate) * up
             }
             const Seg& so = a.swiglu ? a.seg[0] : sg;
+            if (a.tp_world > 1) {
+              pv[it] = v;  // joined with the other GPUs' partials below
+              continue;
+            }
             if (half == 0 && n_idx < so.n) store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
+          }
+        }
+        if (a.tp_world > 1 && rank == 0) {
+          // 1. this GPU's partials of the row block into every GPU's slot [par][tp_rank]
+          const uint32_t par = a.epoch & 1u;
+          const int64_t nb = a.seg[0].n;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            if (it >= a.m) break;
+            const int i = lane + 32 * it;
+            const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
+            const int64_t n_idx = r0 + phys_row(row, a.rg);
+            if (half == 0 && n_idx < nb) {
+              const int64_t off = ((static_cast<int64_t>(par) * a.tp_world + a.tp_rank) * a.m_max + tok) * nb + n_idx;
+              for (int p = 0; p < a.tp_world; ++p) reinterpret_cast<float*>(a.peer[p])[off] = pv[it];
+            }
+          }
+          // 2. publish: the stores above, then the row block's flag on every GPU
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          __syncwarp();
+          const int64_t fo = (static_cast<int64_t>(par) * a.tp_world) * a.tp_nrb + rb;
+          if (lane < a.tp_world)
+            st_release_sys(reinterpret_cast<uint32_t*>(a.peer[lane] + a.tp_flag_off) + fo + a.tp_rank * a.tp_nrb,
+                           a.epoch);
+          // 3. wait for every GPU's partials of this row block (bounded)
+          bool ok2 = true;
+          if (lane < a.tp_world)
+            ok2 = wait_flag_sys(reinterpret_cast<const uint32_t*>(a.peer[a.tp_rank] + a.tp_flag_off) + fo +
+                                    lane * a.tp_nrb, a.epoch);
+          ok2 = __all_sync(0xFFFFFFFFu, ok2);
+          // 4. the sum in rank order (the same bits on every GPU) -> y
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            if (it >= a.m || !ok2) break;
+            const int i = lane + 32 * it;
+            const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
+            const int64_t n_idx = r0 + phys_row(row, a.rg);
+            if (half == 0 && n_idx < nb) {
+              const float* mine = reinterpret_cast<const float*>(a.peer[a.tp_rank]);
+              float v = 0.f;
+              for (int p = 0; p < a.tp_world; ++p)
+                v += mine[((static_cast<int64_t>(par) * a.tp_world + p) * a.m_max + tok) * nb + n_idx];
+              store_y_rt(a.seg[0].y, a.ytype, tok * a.seg[0].ldy + n_idx, v);
+            }
           }
         }
         if (rank == 1) {
@@ -861,9 +936,25 @@ bool gemv_i8_supported(int qtype, int64_t k, int m) {
 // nseg weights of one qtype and K (16-byte aligned bases, row bytes a multiple
 // of 16) against the same activations, one launch.
 // swiglu: nseg = 2 (gate, up) of equal N; y[0] receives silu(x Wg^T) * (x Wu^T).
+// tp (optional): all-reduce y over tp->world GPUs through their exchange buffers.
+struct GemvTp {
+  int world, rank;
+  uint32_t epoch;
+  int64_t m_max;
+  const void* const* bufs;
+};
+size_t gemv_tp_flag_offset(int64_t n, int64_t m_max, int world) {
+  return (static_cast<size_t>(2) * world * m_max * n * 4 + 255) / 256 * 256;
+}
+size_t gemv_tp_buffer_bytes(int64_t n, int64_t m_max, int world) {
+  const int64_t nrb = (n + kRows - 1) / kRows;
+  return gemv_tp_flag_offset(n, m_max, world) + (static_cast<size_t>(2) * world * nrb * 4 + 255) / 256 * 256;
+}
+
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
-                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu) {
+                                   const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu,
+                                   const GemvTp* tp) {
   if (nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
   if (swiglu && (nseg != 2 || n[0] != n[1])) return cudaErrorInvalidValue;
   int dev = 0;
@@ -886,6 +977,17 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   }
   a.nrowblocks = rb;
   a.swiglu = swiglu;
+  a.tp_world = 1;
+  if (tp && tp->world > 1) {
+    if (nseg != 1 || swiglu || tp->world > 8 || m > tp->m_max) return cudaErrorInvalidValue;
+    a.tp_world = tp->world;
+    a.tp_rank = tp->rank;
+    a.epoch = tp->epoch;
+    a.m_max = tp->m_max;
+    a.tp_nrb = rb;
+    a.tp_flag_off = static_cast<int64_t>(gemv_tp_flag_offset(n[0], tp->m_max, tp->world));
+    for (int i = 0; i < tp->world; ++i) a.peer[i] = reinterpret_cast<uint64_t>(tp->bufs[i]);
+  }
   a.k = static_cast<int>(k);
   a.row_bytes = row_bytes;
   a.x = x;

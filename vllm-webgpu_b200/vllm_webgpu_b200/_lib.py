@@ -41,6 +41,9 @@ SIGNATURES = {
     "ggufmm_gemv": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
     "ggufmm_gemv_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP]),
     "ggufmm_gemv_swiglu": (_I, [_VP, _VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
+    "ggufmm_gemv_allreduce_buffer_bytes": (_SZ, [_I64, _I64, _I]),
+    "ggufmm_gemv_allreduce": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _I, _I, _I64,
+                                   ctypes.c_uint32, _VP]),
     "ggufmm_gemm_workspace_size": (_SZ, [_I, _I64, _I64, _I64]),
     "ggufmm_gemm": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
     "ggufmm_mul_mat": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),

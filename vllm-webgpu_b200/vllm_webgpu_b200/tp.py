@@ -11,7 +11,9 @@ vllm_webgpu/v1/worker.py:56-59). This module is the B200 addition:
   superblocks);
 * each rank computes silu(x Wg_r^T) * (x Wu_r^T) and its partial
   y_r = a_r Wd_r^T with the sm_100a kernels, then ONE all-reduce (sum) of the
-  [M, hidden] partials joins the ranks (NCCL over NVLink / NVSwitch).
+  [M, hidden] partials joins the ranks. In decode (M <= 8) the down projection
+  and the all-reduce are one kernel that exchanges the partials through NVLink
+  peer memory (ops.gemv_allreduce); otherwise NCCL over NVLink / NVSwitch.
 
 The matmul callable is injectable so the sharding and the collective can be
 tested on CPU ranks (gloo) against the oracle; on GPUs it is always
@@ -66,6 +68,11 @@ class TensorParallelSwiGLU:
             matmul = mul_mat
         self.matmul = matmul
         self.reduce_dtype = reduce_dtype
+        # decode down projection + all-reduce fused over NVLink (GGUFMM_TP_FUSED=0: NCCL)
+        import os
+        self.fused_allreduce = self.fused_swiglu and reduce_dtype == torch.float32 and \
+            os.environ.get("GGUFMM_TP_FUSED", "1") != "0"
+        self._exchange = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         act = None
@@ -82,9 +89,25 @@ class TensorParallelSwiGLU:
             g = self.matmul(x, self.gate, out_dtype=torch.float32)
             u = self.matmul(x, self.up, out_dtype=torch.float32)
             act = torch.nn.functional.silu(g) * u  # fp32 SwiGLU, fed to down in fp32
+        if self.world > 1 and self.fused_allreduce and act.is_cuda and act.shape[0] <= 8:
+            y = self._down_allreduce(act)
+            if y is not None:
+                return y
         y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
         if self.world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
+
+    def _down_allreduce(self, act: torch.Tensor):
+        """Decode: the down projection and the all-reduce in one kernel over NVLink
+        peer memory (ggufmm_gemv_allreduce); None when the shape is not served."""
+        from . import ops
+        try:
+            if self._exchange is None:
+                self._exchange = ops.PeerExchange(self.down.n, 8, self.group, act.device)
+            return ops.gemv_allreduce(act, self.down, self._exchange, out_dtype=torch.float32)
+        except ValueError:
+            self.fused_allreduce = False  # unsupported shape: NCCL from now on
+            return None
 
     __call__ = forward
