@@ -120,7 +120,7 @@ def test_tp_ffn_two_gpus_fused_allreduce(cuda, tmp_path):
     script = tmp_path / "worker_fused.py"
     script.write_text(WORKER_FUSED.format(root=ROOT))
     out = tmp_path / "y"
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", GGUFMM_TP_FUSED="1")
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
                         "--master-addr", "127.0.0.1", "--master-port", "29534", str(script), str(out)],
                        env=env, capture_output=True, text=True, timeout=600, cwd=ROOT)

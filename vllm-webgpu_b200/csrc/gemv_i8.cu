@@ -633,7 +633,8 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
           }
         }
         if (a.tp_world > 1 && rank == 0) {
-          // 1. this GPU's partials of the row block into every GPU's slot [par][tp_rank]
+          // this GPU's partials of the row block into every GPU's slot [par][tp_rank];
+          // published once per CTA after its last block (one system fence, one flag)
           const uint32_t par = a.epoch & 1u;
           const int64_t nb = a.seg[0].n;
 #pragma unroll
@@ -647,34 +648,6 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
               for (int p = 0; p < a.tp_world; ++p) reinterpret_cast<float*>(a.peer[p])[off] = pv[it];
             }
           }
-          // 2. publish: the stores above, then the row block's flag on every GPU
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          __syncwarp();
-          const int64_t fo = (static_cast<int64_t>(par) * a.tp_world) * a.tp_nrb + rb;
-          if (lane < a.tp_world)
-            st_release_sys(reinterpret_cast<uint32_t*>(a.peer[lane] + a.tp_flag_off) + fo + a.tp_rank * a.tp_nrb,
-                           a.epoch);
-          // 3. wait for every GPU's partials of this row block (bounded)
-          bool ok2 = true;
-          if (lane < a.tp_world)
-            ok2 = wait_flag_sys(reinterpret_cast<const uint32_t*>(a.peer[a.tp_rank] + a.tp_flag_off) + fo +
-                                    lane * a.tp_nrb, a.epoch);
-          ok2 = __all_sync(0xFFFFFFFFu, ok2);
-          // 4. the sum in rank order (the same bits on every GPU) -> y
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            if (it >= a.m || !ok2) break;
-            const int i = lane + 32 * it;
-            const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
-            const int64_t n_idx = r0 + phys_row(row, a.rg);
-            if (half == 0 && n_idx < nb) {
-              const float* mine = reinterpret_cast<const float*>(a.peer[a.tp_rank]);
-              float v = 0.f;
-              for (int p = 0; p < a.tp_world; ++p)
-                v += mine[((static_cast<int64_t>(par) * a.tp_world + p) * a.m_max + tok) * nb + n_idx];
-              store_y_rt(a.seg[0].y, a.ytype, tok * a.seg[0].ldy + n_idx, v);
-            }
-          }
         }
         if (rank == 1) {
           asm volatile("fence.acq_rel.cluster;" ::: "memory");
@@ -686,6 +659,39 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[b]);
+      }
+      if (a.tp_world > 1 && rank == 0 && my_blocks > 0) {
+        // publish this CTA's partials (flag [par][tp_rank][cid] on every GPU), wait for
+        // the other GPUs' flags of the same CTA index (the same row blocks), then the
+        // sums in rank order -- the same bits on every GPU
+        const uint32_t par = a.epoch & 1u;
+        const int64_t nb = a.seg[0].n;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        __syncwarp();
+        const int64_t fo = static_cast<int64_t>(par) * a.tp_world * a.tp_nrb + cid;
+        if (lane < a.tp_world)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.peer[lane] + a.tp_flag_off) + fo + a.tp_rank * a.tp_nrb,
+                         a.epoch);
+        bool ok2 = true;
+        if (lane < a.tp_world)
+          ok2 = wait_flag_sys(reinterpret_cast<const uint32_t*>(a.peer[a.tp_rank] + a.tp_flag_off) + fo +
+                                  lane * a.tp_nrb, a.epoch);
+        ok2 = __all_sync(0xFFFFFFFFu, ok2);
+        const float* mine = reinterpret_cast<const float*>(a.peer[a.tp_rank]);
+        for (int64_t blk = 0; blk < my_blocks && ok2; ++blk) {
+          int64_t r0;
+          block_rows(a, block_of(a, cid, ncl, blk), r0);
+          for (int i = lane; i < kRows * a.m; i += 32) {
+            const int row = i & 15, tok = i >> 4;
+            const int64_t n_idx = r0 + phys_row(row, a.rg);
+            if (n_idx < nb) {
+              float v = 0.f;
+              for (int p = 0; p < a.tp_world; ++p)
+                v += mine[((static_cast<int64_t>(par) * a.tp_world + p) * a.m_max + tok) * nb + n_idx];
+              store_y_rt(a.seg[0].y, a.ytype, tok * a.seg[0].ldy + n_idx, v);
+            }
+          }
+        }
       }
     } else {
       // ---------------- compute ----------------
