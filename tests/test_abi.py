@@ -80,3 +80,36 @@ def test_ops_refuse_cpu_tensors():
         ops.gemv(torch.zeros((1, 256)), w)
     with pytest.raises(ValueError, match="CUDA"):
         ops.dequantize(w)
+
+
+def test_swiglu_and_allreduce_host_validation(lib):
+    """The fused SwiGLU and all-reduce entry points reject bad arguments on the
+    host, before any device query or launch."""
+    from vllm_webgpu_b200 import _lib as L
+    P = 1 << 20
+
+    def sw(qg=P, qu=P, qt=12, n=16, k=256, m=1):
+        return lib.ggufmm_gemv_swiglu(qg, qu, qt, n, k, P, 2, m, k, P, 0, n, None)
+
+    assert sw(qu=None) == L.ERR_ARG
+    assert sw(qg=None) == L.ERR_ARG
+    assert sw(qt=3) == L.ERR_QTYPE
+    assert sw(m=9) == L.ERR_SHAPE
+    assert sw(qu=P + 8) == L.ERR_ALIGN
+
+    bufs = (ctypes.c_void_p * 2)(P, P + 4096)
+
+    def ar(world=2, rank=0, m=1, m_max=8, epoch=1, b=bufs):
+        return lib.ggufmm_gemv_allreduce(P, 12, 16, 256, P, 2, m, 256, P, 0, 16, b, world, rank, m_max, epoch, None)
+
+    assert ar(b=None) == L.ERR_ARG
+    assert ar(world=1) == L.ERR_ARG
+    assert ar(world=9) == L.ERR_ARG
+    assert ar(rank=2) == L.ERR_ARG
+    assert ar(m=4, m_max=2) == L.ERR_ARG
+    assert ar(epoch=0) == L.ERR_ARG
+    assert ar(b=(ctypes.c_void_p * 2)(P, P + 8)) == L.ERR_ALIGN
+    # exchange buffer: 2 parities x world x m_max x n fp32, then 2 x world x row-block flags
+    assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 8, 2) == 2 * 2 * 8 * 8192 * 4 + 2 * 2 * (8192 // 16) * 4
+    assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 9, 2) == 0
+    assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 1, 1) == 0

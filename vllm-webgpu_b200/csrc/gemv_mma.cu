@@ -623,10 +623,10 @@ static int unit_bytes_of(int qt) {
   }
 }
 
-// Compute warps per CTA (8 by default; GGUFMM_GEMV_WARPS=4 for tuning).
+// Compute warps per CTA (8 by default; GGUFMM_GEMV_F16_WARPS=4 for tuning).
 static int compute_warps() {
   static const int w = [] {
-    const char* e = std::getenv("GGUFMM_GEMV_WARPS");
+    const char* e = std::getenv("GGUFMM_GEMV_F16_WARPS");
     const int v = e ? std::atoi(e) : 8;
     return v == 4 ? 4 : 8;
   }();
