@@ -345,12 +345,14 @@ __device__ __forceinline__ const Seg& seg_of(const I8Args& a, int64_t rb) {
 // The j-th row block of cluster / CTA `cid`: plain, every ncl-th block; SwiGLU,
 // every ncl-th PAIR of blocks (gate rows, then the same up rows), so the epilogue
 // holds the gate sums when the up sums arrive.
+template <bool EXT>
 __device__ __forceinline__ int64_t block_of(const I8Args& a, int64_t cid, int64_t ncl, int64_t j) {
-  return a.swiglu ? 2 * (cid + (j >> 1) * ncl) + (j & 1) : cid + j * ncl;
+  return EXT && a.swiglu ? 2 * (cid + (j >> 1) * ncl) + (j & 1) : cid + j * ncl;
 }
 // Segment and first weight row of logical row block lb.
+template <bool EXT>
 __device__ __forceinline__ const Seg& block_rows(const I8Args& a, int64_t lb, int64_t& r0) {
-  if (a.swiglu) {
+  if (EXT && a.swiglu) {
     r0 = (lb >> 1) * kRows;
     return a.seg[lb & 1];
   }
@@ -364,7 +366,8 @@ __device__ __forceinline__ const Seg& block_rows(const I8Args& a, int64_t lb, in
 // become bytes 8t..8t+7.
 __device__ __forceinline__ int q40_pos(int e) { return e < 16 ? (e >> 2) * 8 + (e & 3) : ((e - 16) >> 2) * 8 + 4 + (e & 3); }
 
-template <int QT, int NCG, int NCC, int W>
+// EXT: the SwiGLU / all-reduce epilogue variants (plain GEMVs compile without them)
+template <int QT, int NCG, int NCC, int W, bool EXT>
 __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(const I8Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
@@ -378,8 +381,9 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   // with the K split, the two CTAs of a cluster (consecutive blockIdx.x) share row blocks
   const int rank = a.ksplit == 2 ? static_cast<int>(blockIdx.x & 1) : 0;
   const int64_t cid = blockIdx.x / a.ksplit, ncl = gridDim.x / a.ksplit;
-  const int64_t nunits = a.swiglu ? a.nrowblocks / 2 : a.nrowblocks;  // blocks, or gate/up pairs
-  const int64_t my_blocks = (nunits > cid ? (nunits - 1 - cid) / ncl + 1 : 0) * (a.swiglu ? 2 : 1);
+  const bool pairs = EXT && a.swiglu;
+  const int64_t nunits = pairs ? a.nrowblocks / 2 : a.nrowblocks;  // blocks, or gate/up pairs
+  const int64_t my_blocks = (nunits > cid ? (nunits - 1 - cid) / ncl + 1 : 0) * (pairs ? 2 : 1);
   const int64_t total_pieces = my_blocks * a.nchunks;
   const int units = a.k / kUnitK / a.ksplit;  // this CTA's units along K
   const int ku0 = rank * units;                // ... starting here
@@ -403,10 +407,10 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
   }
 
   auto issue = [&](int64_t p, int s) {
-    const int64_t rb = block_of(a, cid, ncl, p / a.nchunks);
+    const int64_t rb = block_of<EXT>(a, cid, ncl, p / a.nchunks);
     const int ch = static_cast<int>(p % a.nchunks);
     int64_t r0;
-    const Seg& sg = block_rows(a, rb, r0);
+    const Seg& sg = block_rows<EXT>(a, rb, r0);
     const int nr = static_cast<int>((sg.n - r0) < kRows ? (sg.n - r0) : kRows);
     const int nu = min(a.chunk_units, units - ch * a.chunk_units);
     const uint32_t bytes = static_cast<uint32_t>(nu * a.unit_bytes);
@@ -588,18 +592,16 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
         const int b = static_cast<int>(blk & 1);
         if (!mbar_wait(&rfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
-        const int64_t rb = block_of(a, cid, ncl, blk);
+        const int64_t rb = block_of<EXT>(a, cid, ncl, blk);
         const float* rbuf = red + b * (W * a.red_stride);
         int64_t r0;
-        const Seg& sg = block_rows(a, rb, r0);
+        const Seg& sg = block_rows<EXT>(a, rb, r0);
         float* xslot = reinterpret_cast<float*>(smem + a.xchg_off) + b * (8 * kRows);
         if (rank == 1 && blk >= 2 && !mbar_wait_cluster(&xempty[b], static_cast<uint32_t>(((blk >> 1) - 1) & 1))) break;
         if (rank == 0 && a.ksplit == 2 && !mbar_wait_cluster(&xfull[b], static_cast<uint32_t>((blk >> 1) & 1))) break;
         // lane = (row, half): rows on consecutive lanes read consecutive words of
         // the column-major partials (no bank conflicts); each half sums W/2 warps
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          if (it >= a.m) break;
+        auto out_pass = [&](int it) {  // outputs of token `it` (lane = row, half)
           const int i = lane + 32 * it;
           const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
           float v = 0.f;
@@ -614,25 +616,36 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
           if (rank == 1) {
             // this CTA's K half goes to rank 0, which adds it and stores y
             if (half == 0) st_cluster_f32(cluster_addr(xslot + tok * kRows + row, 0), v);
-          } else {
-            if (a.ksplit == 2) v += xslot[tok * kRows + row];
+            return;
+          }
+          if (a.ksplit == 2) v += xslot[tok * kRows + row];
+          if constexpr (EXT) {
             if (a.swiglu) {
               if ((blk & 1) == 0) {
                 gv[it] = v;  // gate: kept until the up rows of the pair
-                continue;
+                return;
               }
               const float g = gv[it];
               v = g / (1.f + __expf(-g)) * v;  // silu(gate) * up
             }
-            const Seg& so = a.swiglu ? a.seg[0] : sg;
             if (a.tp_world > 1) {
               pv[it] = v;  // joined with the other GPUs' partials below
-              continue;
+              return;
             }
-            if (half == 0 && n_idx < so.n) store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
           }
+          const Seg& so = EXT && a.swiglu ? a.seg[0] : sg;
+          if (half == 0 && n_idx < so.n) store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
+        };
+        if constexpr (EXT) {
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {  // registers gv / pv need static indices
+            if (it >= a.m) break;
+            out_pass(it);
+          }
+        } else {
+          for (int it = 0; it < a.m; ++it) out_pass(it);
         }
-        if (a.tp_world > 1 && rank == 0) {
+        if (EXT && a.tp_world > 1 && rank == 0) {
           // this GPU's partials of the row block into every GPU's slot [par][tp_rank];
           // published once per CTA after its last block (one system fence, one flag)
           const uint32_t par = a.epoch & 1u;
@@ -660,7 +673,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[b]);
       }
-      if (a.tp_world > 1 && rank == 0 && my_blocks > 0) {
+      if (EXT && a.tp_world > 1 && rank == 0 && my_blocks > 0) {
         // publish this CTA's partials (flag [par][tp_rank][cid] on every GPU), wait for
         // the other GPUs' flags of the same CTA index (the same row blocks), then the
         // sums in rank order -- the same bits on every GPU
@@ -680,7 +693,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
         const float* mine = reinterpret_cast<const float*>(a.peer[a.tp_rank]);
         for (int64_t blk = 0; blk < my_blocks && ok2; ++blk) {
           int64_t r0;
-          block_rows(a, block_of(a, cid, ncl, blk), r0);
+          block_rows<EXT>(a, block_of<EXT>(a, cid, ncl, blk), r0);
           for (int i = lane; i < kRows * a.m; i += 32) {
             const int row = i & 15, tok = i >> 4;
             const int64_t n_idx = r0 + phys_row(row, a.rg);
@@ -843,10 +856,10 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, int ksplit, I8Arg
 std::mutex g_attr_mu;
 std::set<std::pair<const void*, int>> g_attr_done;
 
-template <int QT, int NCG, int W>
+template <int QT, int NCG, int W, bool EXT>
 cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   constexpr int NCC = NCG == 1 ? 1 : 2;
-  auto fn = gemv_i8_kernel<QT, NCG, NCC, W>;
+  auto fn = gemv_i8_kernel<QT, NCG, NCC, W, EXT>;
   const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs + 4));
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
@@ -876,10 +889,11 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
 
 template <int QT, int W>
 cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
+  const bool ext = a.swiglu || a.tp_world > 1;
   switch (ncg_of(a.m)) {
-    case 1: return launch_t<QT, 1, W>(a, dev, sms, smem_optin, st);
-    case 2: return launch_t<QT, 2, W>(a, dev, sms, smem_optin, st);
-    default: return launch_t<QT, 3, W>(a, dev, sms, smem_optin, st);
+    case 1: return ext ? launch_t<QT, 1, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 1, W, false>(a, dev, sms, smem_optin, st);
+    case 2: return ext ? launch_t<QT, 2, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 2, W, false>(a, dev, sms, smem_optin, st);
+    default: return ext ? launch_t<QT, 3, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 3, W, false>(a, dev, sms, smem_optin, st);
   }
 }
 
