@@ -127,6 +127,18 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
                         void* const* y, int y_dtype, const int64_t* ldy, void* stream);
 
 /*
+ * Which decode GEMV kernel ggufmm_gemv would launch for this shape on the
+ * current device (nothing is launched): GGUFMM_GEMV_INT8 (integer tensor-core
+ * GEMV, Q4_K / Q4_0), GGUFMM_GEMV_F16 (fp16 tensor-core GEMV),
+ * GGUFMM_GEMV_STREAM (CUDA-core streaming GEMV, the fallback), or a negative
+ * GGUFMM_ERR_* code. The reference dispatches one matmul shader per projection
+ * whatever the shape (vllm_webgpu/models/llama.py:276-283); callers use this to
+ * send shapes that only the fallback takes to ggufmm_gemm instead.
+ */
+enum { GGUFMM_GEMV_STREAM = 0, GGUFMM_GEMV_F16 = 1, GGUFMM_GEMV_INT8 = 2 };
+int ggufmm_gemv_kernel(int qtype, int64_t n, int64_t k, int64_t m, int x_dtype);
+
+/*
  * Fused SwiGLU decode GEMV: y[m, n] = silu(sum_k x[m, k] Wg[n, k]) * (sum_k x[m, k] Wu[n, k])
  * for 1 <= M <= 8, the gate and up weights (same qtype, N and K) streamed by one
  * launch and combined in its epilogue (silu(g) = g / (1 + exp(-g)), fp32). It

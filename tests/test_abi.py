@@ -113,3 +113,19 @@ def test_swiglu_and_allreduce_host_validation(lib):
     assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 8, 2) == 2 * 2 * 8 * 8192 * 4 + 2 * 2 * (8192 // 16) * 4
     assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 9, 2) == 0
     assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 1, 1) == 0
+
+
+def test_gemv_kernel_query_host_validation(lib):
+    """ggufmm_gemv_kernel rejects bad shapes, qtypes and dtypes before any device
+    query; on a host without a sm_100 device a valid shape reports a device or
+    CUDA error, never a kernel kind."""
+    from vllm_webgpu_b200 import _lib as L
+    assert lib.ggufmm_gemv_kernel(3, 4096, 4096, 1, 2) == L.ERR_QTYPE
+    assert lib.ggufmm_gemv_kernel(12, 4096, 4096, 9, 2) == L.ERR_SHAPE
+    assert lib.ggufmm_gemv_kernel(12, 4096, 4096, 0, 2) == L.ERR_SHAPE
+    assert lib.ggufmm_gemv_kernel(12, 4096, 4000, 1, 2) == L.ERR_SHAPE
+    assert lib.ggufmm_gemv_kernel(12, 0, 4096, 1, 2) == L.ERR_SHAPE
+    assert lib.ggufmm_gemv_kernel(12, 4096, 4096, 1, 7) == L.ERR_DTYPE
+    import torch
+    if not torch.cuda.is_available():
+        assert lib.ggufmm_gemv_kernel(12, 4096, 4096, 1, 2) < 0

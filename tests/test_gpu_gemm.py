@@ -115,3 +115,26 @@ def test_mul_mat_dispatch_and_shape(cuda):
 def test_gemm_no_device_timeouts(cuda):
     from vllm_webgpu_b200 import _lib
     assert _lib.lib().ggufmm_device_status(1, None) == 0
+
+
+@pytest.mark.parametrize("m,n,k,yd", [(1, 1000, 4096, torch.bfloat16), (8, 4096, 14336, torch.float32),
+                                      (128, 1000, 8192, torch.float16), (40, 8192, 28672, torch.float32)])
+def test_gemm_fused_ksplit_ragged(cuda, m, n, k, yd):
+    """Q4_K at M <= 128 on few weight-row tiles: K is split across CTAs (fp32
+    partials, then an ordered sum); N not a multiple of the 128-row tile."""
+    rows = 256 if n * k > 64 * 2**20 else None
+    # fp16 / bf16 outputs carry their own rounding (2^-11 / 2^-8 of the largest |y|)
+    tol = TOL if yd == torch.float32 else (5e-3 if yd == torch.float16 else 2e-2)
+    assert _check(O.Q4_K, m, n, k, seed=5, rows=rows, ydtype=yd) <= tol
+
+
+def test_gemm_fused_ksplit_deterministic(cuda):
+    """The K split adds its partial sums in a fixed order: repeated calls are
+    bit-identical."""
+    from vllm_webgpu_b200 import ops
+    n, k, m = 4096, 14336, 16
+    w = _wt(O.make_weights(n, k, O.Q4_K, seed=6), O.Q4_K, n, k)
+    x = torch.from_numpy(O.make_activations(m, k, seed=7)).to(torch.bfloat16).cuda()
+    y0 = ops.gemm(x, w, out_dtype=torch.float32)
+    for _ in range(3):
+        assert torch.equal(ops.gemm(x, w, out_dtype=torch.float32), y0)

@@ -137,3 +137,32 @@ def test_gemv_grouped_ragged_and_fallback(cuda):
         torch.cuda.synchronize()
         for r, n, y in zip(raws, ns, ys):
             assert O.rel_err(y.cpu().numpy(), O.matmul_ref(x.float().cpu().numpy(), r, qt, n, k)) <= TOL
+
+
+@pytest.mark.parametrize("m", [2, 4, 8])
+@pytest.mark.parametrize("n,k", [(14336, 4096), (4096, 14336)])
+def test_mul_mat_decode_routing_q4k(cuda, n, k, m):
+    """Q4_K decode through mul_mat, which takes the integer GEMV (one 8-warp CTA
+    per SM when the row blocks fill the GPU, the 2-CTA K split when they do not)
+    or, where only the streaming GEMV would fit, the tcgen05 GEMM."""
+    from vllm_webgpu_b200 import ops
+    raw = O.make_weights(n, k, O.Q4_K, seed=3)
+    x = O.make_activations(m, k, seed=4)
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    w = _wt(raw, O.Q4_K, n, k)
+    kind = ops.gemv_kernel(m, w, xt.dtype)
+    assert kind in (ops.GEMV_INT8, ops.GEMV_F16, ops.GEMV_STREAM)
+    assert ops.gemv_preferred(m, w, xt.dtype) == (kind != ops.GEMV_STREAM)
+    y = ops.mul_mat(xt, w, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref = O.matmul_ref(xt.float().cpu().numpy(), raw, O.Q4_K, n, k)
+    assert O.rel_err(y.float().cpu().numpy(), ref) <= TOL
+
+
+def test_gemv_kernel_kinds(cuda):
+    """The headline decode shapes take the integer tensor-core GEMV."""
+    from vllm_webgpu_b200 import ops
+    from vllm_webgpu_b200.formats import GGUFQuantTensor
+    for n, k, m in [(14336, 4096, 1), (4096, 14336, 1), (14336, 4096, 8)]:
+        w = GGUFQuantTensor(torch.empty((n, k // 256 * 144), dtype=torch.uint8, device="cuda"), O.Q4_K, (n, k))
+        assert ops.gemv_kernel(m, w) == ops.GEMV_INT8, (n, k, m)

@@ -22,7 +22,7 @@ cudaError_t launch_gemv(const void* q, int qtype, int64_t n, int64_t k, const vo
 cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                                  int64_t ldy, cudaStream_t st);
+                                  int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st);
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
 cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -227,6 +227,17 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
   return GGUFMM_OK;
 }
 
+int ggufmm_gemv_kernel(int qtype, int64_t n, int64_t k, int64_t m, int x_dtype) {
+  if (block_of(qtype) == 0) return GGUFMM_ERR_QTYPE;
+  if (n <= 0 || k <= 0 || m < 1 || m > 8 || k % block_of(qtype)) return GGUFMM_ERR_SHAPE;
+  if (elem_size(x_dtype) == 0) return GGUFMM_ERR_DTYPE;
+  const int s = check_device();
+  if (s) return s;
+  if (gemv_i8_supported(qtype, k, static_cast<int>(m))) return GGUFMM_GEMV_INT8;
+  if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype)) return GGUFMM_GEMV_F16;
+  return GGUFMM_GEMV_STREAM;
+}
+
 int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k, const void* x,
                        int x_dtype, int64_t m, int64_t ldx, void* y, int y_dtype, int64_t ldy, void* stream) {
   int s = check_matmul_args(q_gate, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
@@ -312,7 +323,11 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
     // decoded once): only the fp16 activations need scratch. Above one token tile the
     // two-pass path dequantizes each weight once instead of once per token tile.
     cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, workspace, st);
-    if (e == cudaSuccess) e = launch_gemm_fused_q4k(q, workspace, n, m, k, y, y_dtype, ldy, st);
+    // the K split's fp32 partials go where the two-pass path keeps the fp16 weight
+    const size_t x16_bytes = round256(static_cast<size_t>(m) * k * 2);
+    if (e == cudaSuccess)
+      e = launch_gemm_fused_q4k(q, workspace, n, m, k, y, y_dtype, ldy, static_cast<uint8_t*>(workspace) + x16_bytes,
+                                workspace_bytes - x16_bytes, st);
     return cuda_status(e);
   }
   uint8_t* w16 = static_cast<uint8_t*>(workspace);
@@ -331,7 +346,13 @@ int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x
   const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
   const bool gemv_ok = m <= 8 && aligned(q, 16) && row_bytes % 16 == 0 && row_bytes <= 160 * 1024 && aligned(x, 16) &&
                        (ldx * elem_size(x_dtype)) % 16 == 0;
-  if (gemv_ok) return ggufmm_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, stream);
+  // Q4_K shapes that only the streaming GEMV fits run faster on the fused-dequant GEMM,
+  // when the caller passed a workspace for it
+  const bool gemm_better = qtype == kQ4_K && workspace &&
+                           workspace_bytes >= ggufmm_gemm_workspace_size(qtype, m, n, k) &&
+                           ggufmm_gemv_kernel(qtype, n, k, m, x_dtype) == GGUFMM_GEMV_STREAM;
+  if (gemv_ok && !gemm_better)
+    return ggufmm_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, stream);
   return ggufmm_gemm(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, workspace, workspace_bytes, stream);
 }
 

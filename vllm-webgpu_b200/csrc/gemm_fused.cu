@@ -26,6 +26,7 @@
 // Operand precision is that of the two-pass GEMM: the exact fp32 dequantized
 // weight rounded once to fp16, activations in fp16, fp32 accumulation.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -35,8 +36,7 @@
 namespace ggufmm {
 
 constexpr int kFKB = 128;      // weights per k-block (half a Q4_K superblock)
-constexpr int kDqWarps = 8;
-constexpr int kFusedThreads = (6 + kDqWarps) * 32;
+constexpr int kFusedThreads(int dq) { return (6 + dq) * 32; }
 
 template <int BN>
 struct FusedSmem {
@@ -59,11 +59,14 @@ __device__ __forceinline__ float small_uint_to_float(uint32_t v) {
   return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f);
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kFusedThreads, 1)
+// DQ dequantizer warps (8: a thread decodes 64 weights of a k-block, 16: 32).
+// blockIdx.z selects k-blocks [z * kb_per, (z + 1) * kb_per); with part != null
+// the CTA writes its fp32 partial sums to part[z][m][n] instead of y.
+template <int BN, int DQ>
+__global__ void __launch_bounds__(kFusedThreads(DQ), 1)
     gemm_fused_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                           const __grid_constant__ CUtensorMap tm_x, void* __restrict__ y, int ytype, int64_t ldy,
-                          int n, int m, int k) {
+                          int n, int m, int k, float* __restrict__ part, int kb_per) {
   using L = FusedSmem<BN>;
   constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -76,12 +79,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTileW;
-  const int nkb = k / kFKB;
+  const int kb0 = blockIdx.z * kb_per;
+  const int nkb = min(k / kFKB - kb0, kb_per);  // k-blocks of this CTA (>= 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&afull[s], kDqWarps);
+      mbar_init(&afull[s], DQ);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
@@ -101,9 +105,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1)) break;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S, kb = kb0 + i;
+        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
         uint8_t* st = smem + s * L::kStage;
         const int sb = kb >> 1, h = kb & 1;
         mbar_arrive_expect_tx(&full[s], L::kB + L::kHdr + L::kQs);
@@ -117,9 +121,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16<BN>();
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S;
-        const uint32_t par = (kb / S) & 1;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S;
+        const uint32_t par = (i / S) & 1;
         if (!mbar_wait(&full[s], par) || !mbar_wait(&afull[s], par)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t a_addr = smem_u32(smem + s * L::kStage);
@@ -130,7 +134,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
           const uint64_t bdesc = umma_smem_desc(b_addr + atom * (BN * 128));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem_d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || atom > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem_d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i > 0 || atom > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);
       }
@@ -152,22 +156,33 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int mm = m0 + c0 + j;
-            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+            if (mm >= m) continue;
+            if (part)
+              part[(static_cast<int64_t>(blockIdx.z) * m + mm) * n + nrow] = __uint_as_float(r[j]);
+            else
+              store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
           }
         }
       }
     }
   } else {
     // ---------------- dequantizers ----------------
+    // thread (row r, 64-weight half q of the k-block, part sub of that half): with
+    // 16 warps each half is split in two, a thread then owning 16 of its 32 nibble
+    // bytes (output chunks kc = 2 sub, 2 sub + 1 and the same + 4)
+    constexpr int QPT = DQ / 8;    // threads per (row, half)
+    constexpr int KCH = 4 / QPT;   // low-nibble output chunks per thread
     const int dt = (warp - 6) * 32 + lane;
-    const int r = dt & (kTileW - 1), q = dt >> 7;  // row, 64-weight half of the k-block
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      if (!mbar_wait(&full[s], (kb / S) & 1)) break;
+    const int r = dt & (kTileW - 1), qp = dt >> 7;
+    const int q = qp / QPT, sub = qp % QPT;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % S, kb = kb0 + i;
+      if (!mbar_wait(&full[s], (i / S) & 1)) break;
       uint8_t* st = smem + s * L::kStage;
       const uint4 hd = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + r * 16);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32 + 16);
+      const uint8_t* qsrc = st + L::kA + L::kB + L::kHdr + r * 64 + q * 32 + sub * (32 / QPT);
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qsrc);
+      const uint4 q1 = QPT == 1 ? *reinterpret_cast<const uint4*>(qsrc + 16) : q0;
       // nibble chunk c of the superblock: low nibbles = sub-block 2c, high = 2c+1
       const int c = 2 * (kb & 1) + q;
       const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
@@ -183,10 +198,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1)
       const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
       uint8_t* arow = st + q * (kTileW * 128) + r * 128;  // atom q, row r
 #pragma unroll
-      for (int kc = 0; kc < 8; ++kc) {  // 16-byte output chunk: 8 consecutive k of the atom
+      for (int kci = 0; kci < 2 * KCH; ++kci) {  // 16-byte output chunk: 8 consecutive k of the atom
         // k 0..31 = low nibbles of bytes 0..31, k 32..63 = high nibbles
-        const bool hi = kc >= 4;
-        const uint32_t wa = w[(kc & 3) * 2], wb = w[(kc & 3) * 2 + 1];
+        const bool hi = kci >= KCH;
+        const int kk = hi ? kci - KCH : kci;
+        const int kc = sub * KCH + kk + (hi ? 4 : 0);
+        const uint32_t wa = w[kk * 2], wb = w[kk * 2 + 1];
         const int shn = hi ? 4 : 0;
         const float ds = hi ? dsc_hi : dsc_lo, nd = hi ? ndm_hi : ndm_lo;
         uint32_t out[4];
@@ -234,16 +251,60 @@ static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t
 static std::mutex g_fused_attr_mu;
 static std::set<std::pair<const void*, int>> g_fused_attr_done;
 
-template <int BN>
+// y[mm, nn] = sum over z (in order) of part[z][mm][nn]: the K split's partial sums,
+// added in a fixed order so the result does not depend on CTA timing.
+__global__ void fused_splitk_reduce_kernel(const float* __restrict__ part, int ks, int m, int n, void* __restrict__ y,
+                                           int ytype, int64_t ldy) {
+  const int64_t total = static_cast<int64_t>(m) * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int mm = static_cast<int>(i / n), nn = static_cast<int>(i % n);
+    float v = 0.f;
+    for (int z = 0; z < ks; ++z) v += part[z * total + i];
+    store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nn, v);
+  }
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* e = std::getenv(name);
+  return e && e[0] ? std::atoi(e) : dflt;
+}
+
+static int sm_count() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) return 148;
+  return v;
+}
+
+// K slices per tile: one CTA per SM, so a launch of `tiles` tiles split ks ways runs
+// ceil(tiles * ks / sms) waves of 1/ks of the work each, plus a fixed cost per wave
+// (pipeline fill, TMEM allocation, epilogue) taken as 8 k-blocks of work.
+static int pick_fused_ksplit(int64_t tiles, int nkb, int64_t m, int64_t n, size_t part_bytes) {
+  const int forced = env_int("GGUFMM_FUSED_KSPLIT", -1);
+  const int sms = sm_count();
+  int best = 1;
+  double best_cost = 1e30;
+  for (int ks = 1; ks <= 16; ++ks) {
+    if (ks > 1 && (nkb / ks < 4 || static_cast<size_t>(ks) * m * n * 4 > part_bytes)) break;
+    const double waves = static_cast<double>((tiles * ks + sms - 1) / sms);
+    const double cost = waves * (1.0 / ks + 8.0 / nkb);
+    if (cost < best_cost * 0.999) best_cost = cost, best = ks;
+    if (forced > 0 && ks == forced) return ks;
+  }
+  return forced == 0 ? 1 : best;
+}
+
+template <int BN, int DQ>
 static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                   int ytype, int64_t ldy, cudaStream_t st) {
+                                   int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
   using L = FusedSmem<BN>;
   const int64_t row_bytes = k / 256 * 144;
   CUtensorMap mh, mq, mx;
   if (!make_map_q(&mh, q, n, row_bytes, 16) || !make_map_q(&mq, q, n, row_bytes, 64) ||
       !make_map_f16(&mx, x16, m, k, BN))
     return cudaErrorInvalidValue;
-  auto fn = gemm_fused_q4k_kernel<BN>;
+  auto fn = gemm_fused_q4k_kernel<BN, DQ>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -255,19 +316,42 @@ static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, in
       g_fused_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
     }
   }
-  dim3 grid(static_cast<unsigned>((m + BN - 1) / BN), static_cast<unsigned>((n + kTileW - 1) / kTileW));
-  fn<<<grid, kFusedThreads, L::kTotal, st>>>(mh, mq, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
-                                              static_cast<int>(k));
+  const int64_t mt = (m + BN - 1) / BN, nt = (n + kTileW - 1) / kTileW;
+  const int nkb = static_cast<int>(k / kFKB);
+  const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, n, part_bytes) : 1;
+  const int kb_per = (nkb + ks - 1) / ks;
+  const int zs = (nkb + kb_per - 1) / kb_per;  // slices actually used (each >= 1 k-block)
+  float* part = zs > 1 ? static_cast<float*>(part_ws) : nullptr;
+  dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(zs));
+  fn<<<grid, kFusedThreads(DQ), L::kTotal, st>>>(mh, mq, mx, y, ytype, ldy, static_cast<int>(n),
+                                                  static_cast<int>(m), static_cast<int>(k), part, kb_per);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || !part) return e;
+  const int64_t total = m * n;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
+  fused_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, zs, static_cast<int>(m), static_cast<int>(n), y, ytype,
+                                                     ldy);
   return cudaGetLastError();
 }
 
+// 8 dequantizer warps: 16 (half the weights per thread) measured 5-7 % slower at
+// M = 8..128; GGUFMM_FUSED_DQ=16 selects them.
+template <int BN>
+static cudaError_t launch_fused_dq(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
+                                   int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
+  static const int dq = env_int("GGUFMM_FUSED_DQ", 8);
+  return dq == 16 ? launch_fused_bn<BN, 16>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st)
+                  : launch_fused_bn<BN, 8>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+}
+
 // Q4_K weights q (16-byte aligned GGUF blocks [n, k/256*144]) times fp16 activations
-// x16 [m, k] (row-major, 16-byte aligned).
+// x16 [m, k] (row-major, 16-byte aligned). part_ws (256-byte aligned, part_bytes
+// long, may be null) holds the fp32 partial sums when K is split across CTAs.
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                                  int64_t ldy, cudaStream_t st) {
-  if (m <= 32) return launch_fused_bn<32>(q, x16, n, m, k, y, ytype, ldy, st);
-  if (m <= 64) return launch_fused_bn<64>(q, x16, n, m, k, y, ytype, ldy, st);
-  return launch_fused_bn<128>(q, x16, n, m, k, y, ytype, ldy, st);
+                                  int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
+  if (m <= 32) return launch_fused_dq<32>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  if (m <= 64) return launch_fused_dq<64>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  return launch_fused_dq<128>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
 }
 
 cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }

@@ -910,21 +910,30 @@ int forced_warps() {
   }();
   return w;
 }
-bool ksplit_disabled() {
-  static const bool off = [] {
+// GGUFMM_GEMV_KSPLIT=0: never split K; =1: split K whenever the 4-warp shape
+// does not fit (regardless of the row-block count).
+int ksplit_mode() {
+  static const int v = [] {
     const char* e = std::getenv("GGUFMM_GEMV_KSPLIT");
-    return e && e[0] == '0';
+    return e && (e[0] == '0' || e[0] == '1') ? e[0] - '0' : -1;
   }();
-  return off;
+  return v;
 }
+bool ksplit_disabled() { return ksplit_mode() == 0; }
 int smem_of(int W, int optin) { return std::min(optin, W == 4 ? 113 * 1024 : 227 * 1024); }
-int pick_warps(int qt, int64_t k, int m, int optin, I8Args& a) {
+// rowblocks: 16-row blocks of the launch (0 when only asking whether a plan exists).
+int pick_warps(int qt, int64_t k, int m, int optin, I8Args& a, int64_t rowblocks = 0, int sms = 0) {
   const int f = forced_warps();
   if (f) return plan_i8(qt, k, m, smem_of(f, optin), f, 1, a) ? f : 0;
   if (plan_i8(qt, k, m, smem_of(4, optin), 4, 1, a)) return 4;
-  // too large for one half-SM CTA: split K over the two CTAs of a cluster
-  if (!ksplit_disabled() && plan_i8(qt, k, m, smem_of(4, optin), 4, 2, a)) return 4;
-  return plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a) ? 8 : 0;
+  // Too large for one half-SM CTA: split K over the two CTAs of a cluster when
+  // the row blocks are too few to give every SM two of them (the down
+  // projection); with more row blocks one 8-warp CTA per SM is faster (the DSMEM
+  // exchange and the halved copies cost more than the second CTA gains).
+  const bool few_rows = ksplit_mode() == 1 || (rowblocks > 0 && rowblocks < 2 * static_cast<int64_t>(sms));
+  const bool w8 = plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a);
+  if (!ksplit_disabled() && (few_rows || !w8) && plan_i8(qt, k, m, smem_of(4, optin), 4, 2, a)) return 4;
+  return w8 && plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a) ? 8 : 0;
 }
 
 // GGUFMM_GEMV_IMPL=f16 turns this path off (the fp16 tensor-core GEMV then runs).
@@ -982,7 +991,9 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   if (e != cudaSuccess) return e;
   const DevInfo di = device_info(dev);
   I8Args a{};
-  const int W = pick_warps(qtype, k, static_cast<int>(m), di.smem_optin, a);
+  int64_t nrb = 0;
+  for (int i = 0; i < nseg; ++i) nrb += (n[i] + kRows - 1) / kRows;
+  const int W = pick_warps(qtype, k, static_cast<int>(m), di.smem_optin, a, nrb, di.sms);
   if (!W) return cudaErrorInvalidValue;
   const int optin = smem_of(W, di.smem_optin);
   a.nseg = nseg;

@@ -41,9 +41,10 @@ class LlamaB200Model(BaseB200Model):
     def _fused(self, x: torch.Tensor, ws: list, bufs: list) -> bool:
         """One grouped launch for projections that read the same input (decode,
         M <= 8, all GGUF-quantized with one qtype); False if not applicable."""
-        if (x.reshape(-1, x.shape[-1]).shape[0] > ops.GEMV_MAX_M or
+        m = x.reshape(-1, x.shape[-1]).shape[0]
+        if (m > ops.GEMV_MAX_M or
                 not all(isinstance(w, GGUFQuantTensor) for w in ws) or len({w.qtype for w in ws}) != 1
-                or len({b.dtype for b in bufs}) != 1):
+                or len({b.dtype for b in bufs}) != 1 or not ops.gemv_preferred(m, ws[0], x.dtype)):
             return False
         ops.gemv_grouped(x, ws, outs=[b.reshape(-1, w.n) for b, w in zip(bufs, ws)])
         return True

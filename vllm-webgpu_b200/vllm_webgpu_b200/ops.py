@@ -89,6 +89,34 @@ def gemv(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
     return y
 
 
+GEMV_STREAM, GEMV_F16, GEMV_INT8 = 0, 1, 2
+_gemv_kernels: dict = {}
+
+
+def gemv_kernel(m: int, w: GGUFQuantTensor, x_dtype: torch.dtype = torch.bfloat16) -> int:
+    """Which decode GEMV kernel ``gemv`` launches for M tokens against ``w`` on the
+    weight's device: GEMV_INT8, GEMV_F16 or GEMV_STREAM (the CUDA-core fallback)."""
+    dev = _require_cuda(w.data)
+    key = (dev.index, w.qtype, w.n, w.k, m, x_dtype)
+    kind = _gemv_kernels.get(key)
+    if kind is None:
+        with torch.cuda.device(dev):
+            kind = int(_lib.lib().ggufmm_gemv_kernel(w.qtype, w.n, w.k, m, _code(x_dtype)))
+        _lib.check(min(kind, 0), "ggufmm_gemv_kernel")
+        _gemv_kernels[key] = kind
+    return kind
+
+
+def gemv_preferred(m: int, w: GGUFQuantTensor, x_dtype: torch.dtype = torch.bfloat16) -> bool:
+    """Whether the decode GEMV is the faster path for M tokens: M <= 8, and for
+    Q4_K a tensor-core GEMV fits the shape (where only the streaming fallback
+    does, as for M = 8 at K = 14336, the tcgen05 GEMM with fused dequantization
+    is 2-4x faster)."""
+    if not 1 <= m <= GEMV_MAX_M:
+        return False
+    return w.qtype != 12 or gemv_kernel(m, w, x_dtype) != GEMV_STREAM
+
+
 def gemv_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Tensor] | None = None,
                  out_dtype: torch.dtype | None = None) -> list[torch.Tensor]:
     """Decode GEMV of up to 4 weights sharing the activations (fused q/k/v or
@@ -226,7 +254,7 @@ def gemm(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
 
 def mul_mat(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
             out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """y = x @ W^T, GEMV for M <= 8 and tensor-core GEMM above.
+    """y = x @ W^T: GEMV for M <= 8 where gemv_preferred holds, tensor-core GEMM otherwise.
 
     Same contract as vLLM's ``fused_mul_mat_gguf(x, qweight, qweight_type)``
     (vllm/model_executor/layers/quantization/gguf.py:198-230); the leading
@@ -235,7 +263,7 @@ def mul_mat(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None
     lead = x.shape[:-1]
     x2 = _as_2d(x, w.k)
     m = x2.shape[0]
-    if m <= GEMV_MAX_M:
+    if x2.is_cuda and gemv_preferred(m, w, x2.dtype):
         try:
             y = gemv(x2, w, out=out, out_dtype=out_dtype)
         except ValueError:
