@@ -368,21 +368,25 @@ def run_ours(args, rank: int, world: int) -> None:
                "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
                "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
 
-    # batched decode of the same layer (config 3 at M = 16 and 64): every projection through
-    # ops.mul_mat (the model's path above M = 8: the fused-dequant tcgen05 GEMM), replayed
-    # from a CUDA graph over the rotating weight copies
+    # batched decode of the same layer (config 3 at M = 16 and 64): the model's path above
+    # M = 8 -- q/k/v and gate/up as grouped fused-dequant tcgen05 GEMMs, o and down through
+    # ops.mul_mat -- replayed from a CUDA graph over the rotating weight copies
     batched = None
     if not args.no_batched:
-        batched = {"workload": "q4k_llama3_8b_layer_decode", "path": "ops.mul_mat per projection (fused-dequant "
-                   "tcgen05 GEMM, K split where the weight has few 128-row tiles)"}
+        batched = {"workload": "q4k_llama3_8b_layer_decode", "path": "4 launch groups: ops.gemm_grouped (q/k/v, "
+                   "gate/up) and ops.mul_mat (o, down); fused-dequant tcgen05 GEMM, K split where the "
+                   "weights have few 128-row tiles"}
         wbytes = sum(n * k // 256 * 144 for _, n, k in LAYER)
         for mb in (16, 64):
             xb = {kk: torch.randn((mb, kk), generator=g, device=dev).to(torch.bfloat16) for kk in (4096, 14336)}
             yb = [torch.empty((mb, n), dtype=torch.bfloat16, device=dev) for _, n, _ in LAYER]
 
             def bstep(c: int) -> None:
-                for i, (_, n, kk) in enumerate(LAYER):
-                    ops.mul_mat(xb[kk], layers[c][i], out=yb[i])
+                for _, idx, kk in GROUPS:
+                    if len(idx) == 1:
+                        ops.mul_mat(xb[kk], layers[c][idx[0]], out=yb[idx[0]])
+                    else:
+                        ops.gemm_grouped(xb[kk], [layers[c][i] for i in idx], outs=[yb[i] for i in idx])
 
             for i in range(3):
                 bstep(i % copies)

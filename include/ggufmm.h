@@ -127,6 +127,21 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
                         void* const* y, int y_dtype, const int64_t* ldy, void* stream);
 
 /*
+ * GEMM of up to 4 weights that read the same activations (q/k/v, gate/up) at
+ * any M: y_i[m, n_i] = sum_k x[m, k] W_i[n_i, k], all W_i of one qtype and K.
+ * The batched-decode counterpart of ggufmm_gemv_grouped, replacing the same
+ * separate dispatches (vllm_webgpu/models/llama.py:276-283 and 343-348) when
+ * more than 8 tokens are in flight. workspace: at least
+ * ggufmm_gemm_workspace_size(qtype, M, max of n_i, K) bytes, 256-byte aligned.
+ * Q4_K at M <= 128 runs as ONE fused-dequant launch over all the weights' row
+ * tiles (the activations cast once); otherwise one ggufmm_gemm per weight.
+ */
+int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
+                        const void* x, int x_dtype, int64_t m, int64_t ldx,
+                        void* const* y, int y_dtype, const int64_t* ldy,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Which decode GEMV kernel ggufmm_gemv would launch for this shape on the
  * current device (nothing is launched): GGUFMM_GEMV_INT8 (integer tensor-core
  * GEMV, Q4_K / Q4_0), GGUFMM_GEMV_F16 (fp16 tensor-core GEMV),

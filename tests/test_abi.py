@@ -129,3 +129,25 @@ def test_gemv_kernel_query_host_validation(lib):
     import torch
     if not torch.cuda.is_available():
         assert lib.ggufmm_gemv_kernel(12, 4096, 4096, 1, 2) < 0
+
+
+
+def test_gemm_grouped_host_validation(lib):
+    """ggufmm_gemm_grouped rejects bad arguments before touching the device."""
+    from vllm_webgpu_b200 import _lib as L
+    P = 1 << 20
+    qs = (ctypes.c_void_p * 2)(P, P)
+    ns = (ctypes.c_int64 * 2)(256, 128)
+    ys = (ctypes.c_void_p * 2)(P, P)
+    ld = (ctypes.c_int64 * 2)(256, 128)
+
+    def gg(nseg=2, q=qs, n=ns, qt=12, k=256, m=16, y=ys, ldy=ld, ws=P, wsb=1 << 30):
+        return lib.ggufmm_gemm_grouped(nseg, q, n, qt, k, P, 2, m, k, y, 0, ldy, ws, wsb, None)
+
+    assert gg(q=None) == L.ERR_ARG
+    assert gg(nseg=0) == L.ERR_SHAPE
+    assert gg(nseg=5) == L.ERR_SHAPE
+    assert gg(qt=3) == L.ERR_QTYPE
+    assert gg(k=100) == L.ERR_SHAPE
+    assert gg(ws=None) == L.ERR_WORKSPACE
+    assert gg(wsb=1024) == L.ERR_WORKSPACE

@@ -138,3 +138,24 @@ def test_gemm_fused_ksplit_deterministic(cuda):
     y0 = ops.gemm(x, w, out_dtype=torch.float32)
     for _ in range(3):
         assert torch.equal(ops.gemm(x, w, out_dtype=torch.float32), y0)
+
+
+@pytest.mark.parametrize("qt", [O.Q4_K, O.Q8_0], ids=["Q4_K", "Q8_0"])
+@pytest.mark.parametrize("m,shapes", [(16, [(4096, 4096), (1024, 4096), (1024, 4096)]),
+                                      (33, [(1000, 2048), (300, 2048)]),
+                                      (128, [(640, 1024), (640, 1024), (130, 1024), (257, 1024)]),
+                                      (200, [(512, 1024), (384, 1024)])])
+def test_gemm_grouped(cuda, qt, m, shapes):
+    """Weights sharing the activations in one call: Q4_K at M <= 128 is one fused
+    launch over every weight's row tiles (ragged N per weight, K split across CTAs);
+    other types and M > 128 run one GEMM per weight."""
+    from vllm_webgpu_b200 import ops
+    k = shapes[0][1]
+    raws = [O.make_weights(n, k, qt, seed=20 + i) for i, (n, _) in enumerate(shapes)]
+    ws = [_wt(r, qt, n, k) for r, (n, _) in zip(raws, shapes)]
+    x = torch.from_numpy(O.make_activations(m, k, seed=30)).to(torch.bfloat16).cuda()
+    ys = ops.gemm_grouped(x, ws, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    xf = x.float().cpu().numpy()
+    for y, r, (n, _) in zip(ys, raws, shapes):
+        assert O.rel_err(y.cpu().numpy(), O.matmul_ref(xf, r, qt, n, k)) <= TOL, n

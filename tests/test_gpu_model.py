@@ -31,10 +31,11 @@ def _model(cuda):
     return model, raws
 
 
+@pytest.mark.parametrize("m", [1, 16, 64])
 @pytest.mark.parametrize("graph", [False, True], ids=["eager", "graph"])
-def test_layer_linears_match_oracle(cuda, graph):
+def test_layer_linears_match_oracle(cuda, graph, m):
+    """M = 1: grouped decode GEMVs; M = 16 / 64 (batched decode): grouped fused-dequant GEMMs."""
     model, raws = _model(cuda)
-    m = 1
     xs = {nm: torch.from_numpy(O.make_activations(m, k, seed=60 + j)).to(torch.bfloat16).cuda()
           for j, (nm, k) in enumerate((("normed", 512), ("attn_out", 512), ("ffn_normed", 512), ("ffn_act", 1792)))}
     bufs = {p: torch.empty((m, n), dtype=torch.float32, device="cuda") for p, (n, _) in SHAPES.items()}

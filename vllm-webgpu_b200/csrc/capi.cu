@@ -5,6 +5,7 @@
 // the reference's host-side checks (ValueError for bad dimensions in
 // vllm_webgpu/models/llama.py:45-54; FileNotFoundError/RuntimeError for a
 // missing pipeline in vllm_webgpu/webgpu/pipeline.py:25-30).
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
@@ -23,6 +24,9 @@ cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                                   int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st);
+cudaError_t launch_gemm_fused_q4k_grouped(int nseg, const void* const* q, const int64_t* n, const void* x16,
+                                          int64_t m, int64_t k, void* const* y, int ytype, const int64_t* ldy,
+                                          void* part_ws, size_t part_bytes, cudaStream_t st);
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
 cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -335,6 +339,43 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
   if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
   if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st);
+  return cuda_status(e);
+}
+
+int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k, const void* x,
+                        int x_dtype, int64_t m, int64_t ldx, void* const* y, int y_dtype, const int64_t* ldy,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !n || !y || !ldy) return GGUFMM_ERR_ARG;
+  if (nseg < 1 || nseg > 4) return GGUFMM_ERR_SHAPE;
+  int64_t nmax = 0;
+  bool fused = qtype == kQ4_K && m <= 128 && fused_gemm_enabled();
+  for (int i = 0; i < nseg; ++i) {
+    const int s = check_matmul_args(q[i], qtype, n[i], k, x, x_dtype, m, ldx, y[i], y_dtype, ldy[i]);
+    if (s) return s;
+    nmax = std::max(nmax, n[i]);
+    fused = fused && aligned(q[i], 16);
+  }
+  const size_t need = ggufmm_gemm_workspace_size(qtype, m, nmax, k);
+  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(x, elem_size(x_dtype))) return GGUFMM_ERR_ALIGN;
+  for (int i = 0; i < nseg; ++i)
+    if (!aligned(q[i], 2) || !aligned(y[i], elem_size(y_dtype))) return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  if (!fused) {  // one GEMM per weight, sharing the workspace
+    for (int i = 0; i < nseg; ++i) {
+      s = ggufmm_gemm(q[i], qtype, n[i], k, x, x_dtype, m, ldx, y[i], y_dtype, ldy[i], workspace, workspace_bytes,
+                      stream);
+      if (s) return s;
+    }
+    return GGUFMM_OK;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t x16_bytes = round256(static_cast<size_t>(m) * k * 2);
+  cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, workspace, st);
+  if (e == cudaSuccess)
+    e = launch_gemm_fused_q4k_grouped(nseg, q, n, workspace, m, k, y, y_dtype, ldy,
+                                      static_cast<uint8_t*>(workspace) + x16_bytes, workspace_bytes - x16_bytes, st);
   return cuda_status(e);
 }
 

@@ -27,6 +27,7 @@
 // weight rounded once to fp16, activations in fp16, fp32 accumulation.
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -75,14 +76,28 @@ __device__ __forceinline__ float small_uint_to_float(uint32_t v) {
   return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.f);
 }
 
+// Up to kMaxFusedSegs weights of one K that read the same activations (q/k/v,
+// gate/up): segment s owns row tiles [tile0[s], tile0[s + 1]) of the grid's y
+// dimension and global rows [row0[s], row0[s + 1]) of the K split's partials.
+constexpr int kMaxFusedSegs = 4;
+struct FusedSegs {
+  CUtensorMap hdr[kMaxFusedSegs];  // 16-byte Q4_K headers, box 16 B x 128 rows
+  CUtensorMap qs[kMaxFusedSegs];   // nibbles, box 64 B x 128 rows
+  void* y[kMaxFusedSegs];
+  int64_t ldy[kMaxFusedSegs];
+  int n[kMaxFusedSegs];
+  int tile0[kMaxFusedSegs + 1];
+  int row0[kMaxFusedSegs + 1];
+  int nseg;
+};
+
 // DQ dequantizer warps (8: a thread decodes 64 weights of a k-block, 16: 32).
 // blockIdx.z selects k-blocks [z * kb_per, (z + 1) * kb_per); with part != null
-// the CTA writes its fp32 partial sums to part[z][m][n] instead of y.
+// the CTA writes its fp32 partial sums to part[z][m][row0[s] + row] instead of y.
 template <int BN, int DQ, bool X2>
 __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
-    gemm_fused_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
-                          const __grid_constant__ CUtensorMap tm_x, void* __restrict__ y, int ytype, int64_t ldy,
-                          int n, int m, int k, float* __restrict__ part, int kb_per) {
+    gemm_fused_q4k_kernel(const __grid_constant__ FusedSegs sg, const __grid_constant__ CUtensorMap tm_x, int ytype,
+                          int m, int k, float* __restrict__ part, int kb_per) {
   using L = FusedSmem<BN>;
   constexpr int S = L::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -94,7 +109,12 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BN, n0 = blockIdx.y * kTileW;
+  int seg = 0;
+  while (seg + 1 < sg.nseg && static_cast<int>(blockIdx.y) >= sg.tile0[seg + 1]) ++seg;
+  const int m0 = blockIdx.x * BN, n0 = (static_cast<int>(blockIdx.y) - sg.tile0[seg]) * kTileW;
+  const int n = sg.n[seg];
+  const CUtensorMap* tm_hdr = &sg.hdr[seg];
+  const CUtensorMap* tm_qs = &sg.qs[seg];
   const int kb0 = blockIdx.z * kb_per;
   const int nkb = min(k / kFKB - kb0, kb_per);  // k-blocks of this CTA (>= 1)
 
@@ -127,8 +147,8 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
         uint8_t* st = smem + s * L::kStage;
         const int sb = kb >> 1, h = kb & 1;
         mbar_arrive_expect_tx(&full[s], L::kB + L::kHdr + L::kQs);
-        tma_load_2d(st + L::kA + L::kB, &tm_hdr, 144 * sb, n0, &full[s]);
-        tma_load_2d(st + L::kA + L::kB + L::kHdr, &tm_qs, 144 * sb + 16 + 64 * h, n0, &full[s]);
+        tma_load_2d(st + L::kA + L::kB, tm_hdr, 144 * sb, n0, &full[s]);
+        tma_load_2d(st + L::kA + L::kB + L::kHdr, tm_qs, 144 * sb + 16 + 64 * h, n0, &full[s]);
         tma_load_2d(st + L::kA, &tm_x, kb * kFKB, m0, &full[s]);
         tma_load_2d(st + L::kA + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
       }
@@ -163,6 +183,9 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
       const int nrow = n0 + quad * 32 + lane;
+      void* const y = sg.y[seg];
+      const int64_t ldy = sg.ldy[seg];
+      const int64_t ntot = sg.row0[sg.nseg], grow = sg.row0[seg] + nrow;
       const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -174,7 +197,7 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
             const int mm = m0 + c0 + j;
             if (mm >= m) continue;
             if (part)
-              part[(static_cast<int64_t>(blockIdx.z) * m + mm) * n + nrow] = __uint_as_float(r[j]);
+              part[(static_cast<int64_t>(blockIdx.z) * m + mm) * ntot + grow] = __uint_as_float(r[j]);
             else
               store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
           }
@@ -272,17 +295,25 @@ static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t
 static std::mutex g_fused_attr_mu;
 static std::set<std::pair<const void*, int>> g_fused_attr_done;
 
-// y[mm, nn] = sum over z (in order) of part[z][mm][nn]: the K split's partial sums,
-// added in a fixed order so the result does not depend on CTA timing.
-__global__ void fused_splitk_reduce_kernel(const float* __restrict__ part, int ks, int m, int n, void* __restrict__ y,
-                                           int ytype, int64_t ldy) {
-  const int64_t total = static_cast<int64_t>(m) * n;
+// y_s[mm, row] = sum over z (in order) of part[z][mm][row0[s] + row]: the K split's
+// partial sums, added in a fixed order so the result does not depend on CTA timing.
+struct ReduceSegs {
+  void* y[kMaxFusedSegs];
+  int64_t ldy[kMaxFusedSegs];
+  int row0[kMaxFusedSegs + 1];
+  int nseg;
+};
+__global__ void fused_splitk_reduce_kernel(const float* __restrict__ part, int ks, int m, ReduceSegs rs, int ytype) {
+  const int ntot = rs.row0[rs.nseg];
+  const int64_t total = static_cast<int64_t>(m) * ntot;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int mm = static_cast<int>(i / n), nn = static_cast<int>(i % n);
+    const int mm = static_cast<int>(i / ntot), g = static_cast<int>(i % ntot);
+    int sgi = 0;
+    while (sgi + 1 < rs.nseg && g >= rs.row0[sgi + 1]) ++sgi;
     float v = 0.f;
     for (int z = 0; z < ks; ++z) v += part[z * total + i];
-    store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nn, v);
+    store_y_rt(rs.y[sgi], ytype, static_cast<int64_t>(mm) * rs.ldy[sgi] + (g - rs.row0[sgi]), v);
   }
 }
 
@@ -317,14 +348,27 @@ static int pick_fused_ksplit(int64_t tiles, int nkb, int64_t m, int64_t n, size_
 }
 
 template <int BN, int DQ, bool X2>
-static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                   int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
+static cudaError_t launch_fused_bn(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
+                                   int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
+                                   size_t part_bytes, cudaStream_t st) {
   using L = FusedSmem<BN>;
   const int64_t row_bytes = k / 256 * 144;
-  CUtensorMap mh, mq, mx;
-  if (!make_map_q(&mh, q, n, row_bytes, 16) || !make_map_q(&mq, q, n, row_bytes, 64) ||
-      !make_map_f16(&mx, x16, m, k, BN))
-    return cudaErrorInvalidValue;
+  FusedSegs sg;
+  memset(&sg, 0, sizeof(sg));
+  ReduceSegs rs;
+  memset(&rs, 0, sizeof(rs));
+  sg.nseg = rs.nseg = nseg;
+  for (int i = 0; i < nseg; ++i) {
+    if (!make_map_q(&sg.hdr[i], q[i], n[i], row_bytes, 16) || !make_map_q(&sg.qs[i], q[i], n[i], row_bytes, 64))
+      return cudaErrorInvalidValue;
+    sg.y[i] = rs.y[i] = y[i];
+    sg.ldy[i] = rs.ldy[i] = ldy[i];
+    sg.n[i] = static_cast<int>(n[i]);
+    sg.tile0[i + 1] = sg.tile0[i] + static_cast<int>((n[i] + kTileW - 1) / kTileW);
+    sg.row0[i + 1] = rs.row0[i + 1] = sg.row0[i] + static_cast<int>(n[i]);
+  }
+  CUtensorMap mx;
+  if (!make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
   auto fn = gemm_fused_q4k_kernel<BN, DQ, X2>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -337,21 +381,20 @@ static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, in
       g_fused_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
     }
   }
-  const int64_t mt = (m + BN - 1) / BN, nt = (n + kTileW - 1) / kTileW;
+  const int64_t mt = (m + BN - 1) / BN, nt = sg.tile0[nseg], ntot = sg.row0[nseg];
   const int nkb = static_cast<int>(k / kFKB);
-  const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, n, part_bytes) : 1;
+  const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, ntot, part_bytes) : 1;
   const int kb_per = (nkb + ks - 1) / ks;
   const int zs = (nkb + kb_per - 1) / kb_per;  // slices actually used (each >= 1 k-block)
   float* part = zs > 1 ? static_cast<float*>(part_ws) : nullptr;
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(zs));
-  fn<<<grid, kFusedThreads(DQ), L::kTotal, st>>>(mh, mq, mx, y, ytype, ldy, static_cast<int>(n),
-                                                  static_cast<int>(m), static_cast<int>(k), part, kb_per);
+  fn<<<grid, kFusedThreads(DQ), L::kTotal, st>>>(sg, mx, ytype, static_cast<int>(m), static_cast<int>(k), part,
+                                                  kb_per);
   e = cudaGetLastError();
   if (e != cudaSuccess || !part) return e;
-  const int64_t total = m * n;
+  const int64_t total = m * ntot;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
-  fused_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, zs, static_cast<int>(m), static_cast<int>(n), y, ytype,
-                                                     ldy);
+  fused_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, zs, static_cast<int>(m), rs, ytype);
   return cudaGetLastError();
 }
 
@@ -360,23 +403,33 @@ static cudaError_t launch_fused_bn(const void* q, const void* x16, int64_t n, in
 // 5-7 % slower; GGUFMM_FUSED_DQ=16 selects them (scalar), GGUFMM_FUSED_F32X2=0 the
 // scalar 8-warp variant.
 template <int BN>
-static cudaError_t launch_fused_dq(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                   int ytype, int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
+static cudaError_t launch_fused_dq(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
+                                   int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
+                                   size_t part_bytes, cudaStream_t st) {
   static const int dq = env_int("GGUFMM_FUSED_DQ", 8);
   static const int x2 = env_int("GGUFMM_FUSED_F32X2", 1);
-  if (dq == 16) return launch_fused_bn<BN, 16, false>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  return x2 ? launch_fused_bn<BN, 8, true>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st)
-            : launch_fused_bn<BN, 8, false>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  if (dq == 16)
+    return launch_fused_bn<BN, 16, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  return x2 ? launch_fused_bn<BN, 8, true>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st)
+            : launch_fused_bn<BN, 8, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
 }
 
-// Q4_K weights q (16-byte aligned GGUF blocks [n, k/256*144]) times fp16 activations
-// x16 [m, k] (row-major, 16-byte aligned). part_ws (256-byte aligned, part_bytes
-// long, may be null) holds the fp32 partial sums when K is split across CTAs.
+// nseg (1..4) Q4_K weights q[i] (16-byte aligned GGUF blocks [n[i], k/256*144]) times
+// fp16 activations x16 [m, k] (row-major, 16-byte aligned) into y[i] [m, n[i]] with
+// row stride ldy[i]. part_ws (256-byte aligned, part_bytes long, may be null) holds
+// the fp32 partial sums when K is split across CTAs.
+cudaError_t launch_gemm_fused_q4k_grouped(int nseg, const void* const* q, const int64_t* n, const void* x16,
+                                          int64_t m, int64_t k, void* const* y, int ytype, const int64_t* ldy,
+                                          void* part_ws, size_t part_bytes, cudaStream_t st) {
+  if (nseg < 1 || nseg > kMaxFusedSegs) return cudaErrorInvalidValue;
+  if (m <= 32) return launch_fused_dq<32>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  if (m <= 64) return launch_fused_dq<64>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  return launch_fused_dq<128>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+}
+
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                                   int64_t ldy, void* part_ws, size_t part_bytes, cudaStream_t st) {
-  if (m <= 32) return launch_fused_dq<32>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  if (m <= 64) return launch_fused_dq<64>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  return launch_fused_dq<128>(q, x16, n, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  return launch_gemm_fused_q4k_grouped(1, &q, &n, x16, m, k, &y, ytype, &ldy, part_ws, part_bytes, st);
 }
 
 cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }

@@ -39,14 +39,18 @@ class LlamaB200Model(BaseB200Model):
         return out
 
     def _fused(self, x: torch.Tensor, ws: list, bufs: list) -> bool:
-        """One grouped launch for projections that read the same input (decode,
-        M <= 8, all GGUF-quantized with one qtype); False if not applicable."""
+        """One grouped launch for projections that read the same input (all
+        GGUF-quantized with one qtype): the grouped decode GEMV where it is the
+        faster path, else the grouped GEMM; False if not applicable."""
         m = x.reshape(-1, x.shape[-1]).shape[0]
-        if (m > ops.GEMV_MAX_M or
-                not all(isinstance(w, GGUFQuantTensor) for w in ws) or len({w.qtype for w in ws}) != 1
-                or len({b.dtype for b in bufs}) != 1 or not ops.gemv_preferred(m, ws[0], x.dtype)):
+        if (not all(isinstance(w, GGUFQuantTensor) for w in ws) or len({w.qtype for w in ws}) != 1
+                or len({b.dtype for b in bufs}) != 1 or not x.is_cuda):
             return False
-        ops.gemv_grouped(x, ws, outs=[b.reshape(-1, w.n) for b, w in zip(bufs, ws)])
+        outs = [b.reshape(-1, w.n) for b, w in zip(bufs, ws)]
+        if ops.gemv_preferred(m, ws[0], x.dtype):
+            ops.gemv_grouped(x, ws, outs=outs)
+        else:
+            ops.gemm_grouped(x, ws, outs=outs)
         return True
 
     def project_qkv(self, layer: int, normed: torch.Tensor, q_buf, k_buf, v_buf):

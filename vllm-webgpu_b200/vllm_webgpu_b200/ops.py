@@ -227,7 +227,8 @@ _workspaces: dict[int, torch.Tensor] = {}
 
 
 def workspace_for(w: GGUFQuantTensor, m: int) -> torch.Tensor:
-    """A cached per-device scratch buffer large enough for ggufmm_gemm."""
+    """A cached per-device scratch buffer large enough for ggufmm_gemm (and for
+    ggufmm_gemm_grouped when w is the group's weight with the largest N)."""
     need = int(_lib.lib().ggufmm_gemm_workspace_size(w.qtype, m, w.n, w.k))
     idx = w.data.device.index
     ws = _workspaces.get(idx)
@@ -250,6 +251,37 @@ def gemm(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
                                     ws.data_ptr(), ws.numel(), _stream(dev))
     _lib.check(st, "ggufmm_gemm")
     return y
+
+
+def gemm_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Tensor] | None = None,
+                 out_dtype: torch.dtype | None = None) -> list[torch.Tensor]:
+    """GEMM of up to 4 weights sharing the activations (q/k/v or gate/up) at any M;
+    Q4_K at M <= 128 is one fused-dequant launch over all of them."""
+    if not 1 <= len(ws) <= 4:
+        raise ValueError("gemm_grouped takes 1 to 4 weights")
+    k, qt = ws[0].k, ws[0].qtype
+    if any(w.k != k or w.qtype != qt for w in ws):
+        raise ValueError("grouped weights must share K and the quantization type")
+    dev = _require_cuda(x, *[w.data for w in ws])
+    x2 = _as_2d(x, k)
+    if outs is None:
+        outs = [None] * len(ws)
+    ys = [_out(x2, w.n, o, out_dtype) for w, o in zip(ws, outs)]
+    if len({y.dtype for y in ys}) != 1:
+        raise ValueError("grouped outputs must share a dtype")
+    import ctypes
+    nseg = len(ws)
+    wsp = workspace_for(max(ws, key=lambda w: w.n), x2.shape[0])
+    qs = (ctypes.c_void_p * nseg)(*[w.data.data_ptr() for w in ws])
+    ns = (ctypes.c_int64 * nseg)(*[w.n for w in ws])
+    yp = (ctypes.c_void_p * nseg)(*[y.data_ptr() for y in ys])
+    ld = (ctypes.c_int64 * nseg)(*[y.stride(0) for y in ys])
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemm_grouped(nseg, qs, ns, qt, k, x2.data_ptr(), _code(x2.dtype), x2.shape[0],
+                                            x2.stride(0), yp, _code(ys[0].dtype), ld, wsp.data_ptr(), wsp.numel(),
+                                            _stream(dev))
+    _lib.check(st, "ggufmm_gemm_grouped")
+    return ys
 
 
 def mul_mat(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
