@@ -142,6 +142,19 @@ int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qt
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Decode GEMV with the residual add in its epilogue: y = x W^T + resid for
+ * 1 <= M <= 8, Q4_K / Q4_0 with K a multiple of 256 (GGUFMM_ERR_SHAPE /
+ * GGUFMM_ERR_QTYPE otherwise, nothing launched). resid has y_dtype and row
+ * stride ldr (>= N) and may be y itself (in place). Replaces the o / down
+ * projection plus the add shader that follows it (vllm_webgpu/models/llama.py:329-335
+ * and 357-363, shaders/generic/add.wgsl): the sum is formed in fp32 and rounded
+ * once into y.
+ */
+int ggufmm_gemv_residual(const void* q, int qtype, int64_t n, int64_t k,
+                         const void* x, int x_dtype, int64_t m, int64_t ldx,
+                         void* y, int y_dtype, int64_t ldy, const void* resid, int64_t ldr, void* stream);
+
+/*
  * Which decode GEMV kernel ggufmm_gemv would launch for this shape on the
  * current device (nothing is launched): GGUFMM_GEMV_INT8 (integer tensor-core
  * GEMV, Q4_K / Q4_0), GGUFMM_GEMV_F16 (fp16 tensor-core GEMV),

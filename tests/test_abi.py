@@ -151,3 +151,19 @@ def test_gemm_grouped_host_validation(lib):
     assert gg(k=100) == L.ERR_SHAPE
     assert gg(ws=None) == L.ERR_WORKSPACE
     assert gg(wsb=1024) == L.ERR_WORKSPACE
+
+
+
+def test_gemv_residual_host_validation(lib):
+    """ggufmm_gemv_residual rejects bad arguments before touching the device."""
+    from vllm_webgpu_b200 import _lib as L
+    P = 1 << 20
+
+    def gr(r=P, m=1, ldr=16, qt=12, yd=0):
+        return lib.ggufmm_gemv_residual(P, qt, 16, 256, P, 2, m, 256, P, yd, 16, r, ldr, None)
+
+    assert gr(r=None) == L.ERR_ARG
+    assert gr(m=9) == L.ERR_SHAPE
+    assert gr(ldr=15) == L.ERR_SHAPE
+    assert gr(qt=3) == L.ERR_QTYPE
+    assert gr(r=P + 2) == L.ERR_ALIGN

@@ -52,7 +52,10 @@ def _worker(rank, world, port, x, q):
         g, u, d = _weights()
         ffn = TensorParallelSwiGLU(g, u, d, rank=rank, world=world, matmul=_oracle_matmul)
         y = ffn(x)
-        q.put((rank, y.numpy()))
+        # the residual rides on rank 0's partial only: the sum carries it once
+        res = torch.from_numpy(O.make_activations(M, H, seed=9))
+        yr = ffn(x, residual=res)
+        q.put((rank, (y.numpy(), yr.numpy())))
     finally:
         dist.destroy_process_group()
 
@@ -71,8 +74,10 @@ def test_tp_ffn_matches_unsharded(world):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    res = O.make_activations(M, H, seed=9)
     for r in range(world):
-        assert O.rel_err(outs[r], ref) < 1e-5
+        assert O.rel_err(outs[r][0], ref) < 1e-5
+        assert O.rel_err(outs[r][1], ref + res) < 1e-5
 
 
 def test_shard_ranges_and_errors():

@@ -40,7 +40,7 @@ bool gemv_i8_supported(int qtype, int64_t k, int m);
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
                                    const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu,
-                                   const struct GemvTp* tp);
+                                   const struct GemvTp* tp, const void* resid = nullptr, int64_t ldr = 0);
 struct GemvTp {
   int world, rank;
   uint32_t epoch;
@@ -292,6 +292,24 @@ int ggufmm_gemv_allreduce(const void* q, int qtype, int64_t n, int64_t k, const 
   const GemvTp tp{world, rank, epoch, m_max, peer_bufs};
   return cuda_status(launch_gemv_i8_grouped(1, &q, &n, qtype, k, x, x_dtype, m, ldx, &y, y_dtype, &ldy, row_bytes,
                                             static_cast<cudaStream_t>(stream), 0, &tp));
+}
+
+int ggufmm_gemv_residual(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                         int64_t ldx, void* y, int y_dtype, int64_t ldy, const void* resid, int64_t ldr, void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (!resid) return GGUFMM_ERR_ARG;
+  if (m > 8 || ldr < n) return GGUFMM_ERR_SHAPE;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  if (!aligned(q, 16) || row_bytes % 16 || !aligned(x, 16) || (ldx * elem_size(x_dtype)) % 16 ||
+      !aligned(y, elem_size(y_dtype)) || !aligned(resid, elem_size(y_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  s = check_device();
+  if (s) return s;
+  if (!gemv_i8_supported(qtype, k, static_cast<int>(m)))
+    return qtype == GGUFMM_Q4_K || qtype == GGUFMM_Q4_0 ? GGUFMM_ERR_SHAPE : GGUFMM_ERR_QTYPE;
+  return cuda_status(launch_gemv_i8_grouped(1, &q, &n, qtype, k, x, x_dtype, m, ldx, &y, y_dtype, &ldy, row_bytes,
+                                            static_cast<cudaStream_t>(stream), 0, nullptr, resid, ldr));
 }
 
 static size_t round256(size_t v) { return (v + 255) / 256 * 256; }

@@ -176,4 +176,10 @@ __device__ __forceinline__ void store_y_rt(void* base, int ytype, int64_t idx, f
   else store_y<GGUFMM_BF16>(base, idx, v);
 }
 
+__device__ __forceinline__ float load_y_rt(const void* base, int ytype, int64_t idx) {
+  if (ytype == GGUFMM_F32) return static_cast<const float*>(base)[idx];
+  if (ytype == GGUFMM_F16) return __half2float(static_cast<const __half*>(base)[idx]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx]);
+}
+
 }  // namespace ggufmm

@@ -86,6 +86,8 @@ struct I8Args {
   int red_stride;    // floats per warp in one reduction buffer
   int ksplit;        // 1, or 2: K halves on the two CTAs of a cluster, partials joined in rank 0
   int swiglu;        // segments 0 (gate) and 1 (up) of equal N: y = silu(gate) * up into segment 0's y
+  const void* resid; // optional residual added to segment 0's y (y's dtype, row stride ldr; may alias y)
+  int64_t ldr;
   // all-reduce over tp_world GPUs through peer memory (tp_world > 1): every GPU's
   // exchange buffer, [2 parities][tp_world sources][m_max][n] fp32 partials then
   // [2][tp_world][row blocks] u32 flags; y = the sum of the partials
@@ -634,7 +636,10 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
             }
           }
           const Seg& so = EXT && a.swiglu ? a.seg[0] : sg;
-          if (half == 0 && n_idx < so.n) store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
+          if (half == 0 && n_idx < so.n) {
+            if (EXT && a.resid) v += load_y_rt(a.resid, a.ytype, tok * a.ldr + n_idx);
+            store_y_rt(so.y, a.ytype, tok * so.ldy + n_idx, v);
+          }
         };
         if constexpr (EXT) {
 #pragma unroll
@@ -701,6 +706,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
               float v = 0.f;
               for (int p = 0; p < a.tp_world; ++p)
                 v += mine[((static_cast<int64_t>(par) * a.tp_world + p) * a.m_max + tok) * nb + n_idx];
+              if (a.resid) v += load_y_rt(a.resid, a.ytype, tok * a.ldr + n_idx);
               store_y_rt(a.seg[0].y, a.ytype, tok * a.seg[0].ldy + n_idx, v);
             }
           }
@@ -889,7 +895,7 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
 
 template <int QT, int W>
 cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
-  const bool ext = a.swiglu || a.tp_world > 1;
+  const bool ext = a.swiglu || a.tp_world > 1 || a.resid;
   switch (ncg_of(a.m)) {
     case 1: return ext ? launch_t<QT, 1, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 1, W, false>(a, dev, sms, smem_optin, st);
     case 2: return ext ? launch_t<QT, 2, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 2, W, false>(a, dev, sms, smem_optin, st);
@@ -966,6 +972,8 @@ bool gemv_i8_supported(int qtype, int64_t k, int m) {
 // of 16) against the same activations, one launch.
 // swiglu: nseg = 2 (gate, up) of equal N; y[0] receives silu(x Wg^T) * (x Wu^T).
 // tp (optional): all-reduce y over tp->world GPUs through their exchange buffers.
+// resid (optional, nseg = 1, no swiglu): y = x W^T + resid, resid in y's dtype with row stride ldr
+// (it may be y itself for an in-place residual add).
 struct GemvTp {
   int world, rank;
   uint32_t epoch;
@@ -983,8 +991,9 @@ size_t gemv_tp_buffer_bytes(int64_t n, int64_t m_max, int world) {
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
                                    const int64_t* ldy, int64_t row_bytes, cudaStream_t st, int swiglu,
-                                   const GemvTp* tp) {
+                                   const GemvTp* tp, const void* resid, int64_t ldr) {
   if (nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+  if (resid && (nseg != 1 || swiglu)) return cudaErrorInvalidValue;
   if (swiglu && (nseg != 2 || n[0] != n[1])) return cudaErrorInvalidValue;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1008,6 +1017,8 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   }
   a.nrowblocks = rb;
   a.swiglu = swiglu;
+  a.resid = resid;
+  a.ldr = ldr;
   a.tp_world = 1;
   if (tp && tp->world > 1) {
     if (nseg != 1 || swiglu || tp->world > 8 || m > tp->m_max) return cudaErrorInvalidValue;

@@ -41,6 +41,7 @@ SIGNATURES = {
     "ggufmm_gemv": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
     "ggufmm_gemv_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP]),
     "ggufmm_gemm_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP, _SZ, _VP]),
+    "ggufmm_gemv_residual": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _I64, _VP]),
     "ggufmm_gemv_kernel": (_I, [_I, _I64, _I64, _I64, _I]),
     "ggufmm_gemv_swiglu": (_I, [_VP, _VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
     "ggufmm_gemv_allreduce_buffer_bytes": (_SZ, [_I64, _I64, _I]),

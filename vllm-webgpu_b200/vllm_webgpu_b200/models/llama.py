@@ -60,8 +60,22 @@ class LlamaB200Model(BaseB200Model):
                 self._linear(normed, w, buf)
         return q_buf, k_buf, v_buf
 
-    def project_o(self, layer: int, attn_out: torch.Tensor, out: torch.Tensor):
-        return self._linear(attn_out, self._w(layer, "o"), out)
+    def _linear_residual(self, x: torch.Tensor, w, out: torch.Tensor, residual):
+        """out = x W^T (+ residual): the reference's projection followed by its add
+        shader (llama.py:329-335, 357-363). Decode on the integer GEMV adds the
+        residual in the GEMV's epilogue (one launch, rounded once); otherwise the
+        projection is followed by an elementwise add."""
+        if residual is None:
+            return self._linear(x, w, out)
+        if isinstance(w, GGUFQuantTensor) and ops.residual_fusable(x, w) and out.dtype == residual.dtype:
+            ops.gemv_residual(x, w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
+            return out
+        self._linear(x, w, out)
+        out.add_(residual)
+        return out
+
+    def project_o(self, layer: int, attn_out: torch.Tensor, out: torch.Tensor, residual=None):
+        return self._linear_residual(attn_out, self._w(layer, "o"), out, residual)
 
     def project_gate_up(self, layer: int, ffn_normed: torch.Tensor, gate_buf, up_buf):
         ws = [self._w(layer, "gate"), self._w(layer, "up")]
@@ -70,8 +84,8 @@ class LlamaB200Model(BaseB200Model):
             self._linear(ffn_normed, ws[1], up_buf)
         return gate_buf, up_buf
 
-    def project_down(self, layer: int, ffn_act: torch.Tensor, out: torch.Tensor):
-        return self._linear(ffn_act, self._w(layer, "down"), out)
+    def project_down(self, layer: int, ffn_act: torch.Tensor, out: torch.Tensor, residual=None):
+        return self._linear_residual(ffn_act, self._w(layer, "down"), out, residual)
 
     def project_ffn_act(self, layer: int, ffn_normed: torch.Tensor, act_buf: torch.Tensor) -> torch.Tensor:
         """The FFN activation silu(gate) * up into ``act_buf``: in decode one fused

@@ -170,6 +170,34 @@ def gemv_swiglu(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor, out
     return y
 
 
+def residual_fusable(x: torch.Tensor, w: GGUFQuantTensor) -> bool:
+    """Whether gemv_residual handles these operands (decode M on the integer GEMV)."""
+    m = x.numel() // max(x.shape[-1], 1)
+    return (x.is_cuda and w.qtype in (2, 12) and w.k % 256 == 0 and x.shape[-1] == w.k
+            and gemv_preferred(m, w, x.dtype) and gemv_kernel(m, w, x.dtype) == GEMV_INT8)
+
+
+def gemv_residual(x: torch.Tensor, w: GGUFQuantTensor, residual: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode GEMV with the residual add fused: out = x W^T + residual, one launch,
+    the sum rounded once into out's dtype (= residual's). ``out`` may be
+    ``residual`` itself (in place)."""
+    dev = _require_cuda(x, w.data, residual)
+    x2 = _as_2d(x, w.k)
+    r2 = residual.reshape(-1, w.n) if residual.dim() != 2 else residual
+    if r2.shape != (x2.shape[0], w.n) or r2.stride(1) != 1:
+        raise ValueError(f"residual must be [{x2.shape[0]}, {w.n}] with unit column stride")
+    y = _out(x2, w.n, out, r2.dtype)
+    if y.dtype != r2.dtype:
+        raise ValueError("out and residual must share a dtype")
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemv_residual(w.data.data_ptr(), w.qtype, w.n, w.k, x2.data_ptr(), _code(x2.dtype),
+                                             x2.shape[0], x2.stride(0), y.data_ptr(), _code(y.dtype), y.stride(0),
+                                             r2.data_ptr(), r2.stride(0), _stream(dev))
+    _lib.check(st, "ggufmm_gemv_residual")
+    return y
+
+
 class PeerExchange:
     """Exchange buffers for ``gemv_allreduce`` on every GPU of a process group:
     one symmetric-memory allocation per GPU (``torch.distributed._symmetric_memory``,

@@ -76,7 +76,11 @@ class TensorParallelSwiGLU:
             os.environ.get("GGUFMM_TP_FUSED", "0") == "1"
         self._exchange = None
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """The FFN output, plus ``residual`` when given (the reference's final add,
+        llama.py:362-363): rank 0 adds it to its partial before the all-reduce, so the
+        sum carries it once -- in the down projection's epilogue when that GEMV runs on
+        the integer tensor cores with the residual in the reduce dtype."""
         act = None
         if self.fused_swiglu and x.is_cuda:
             from . import ops
@@ -94,8 +98,17 @@ class TensorParallelSwiGLU:
         if self.world > 1 and self.fused_allreduce and act.is_cuda and act.shape[0] <= 8:
             y = self._down_allreduce(act)
             if y is not None:
-                return y
-        y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
+                return y if residual is None else y.add_(residual)
+        y = None
+        add_here = residual is not None and self.rank == 0
+        if add_here and self.fused_swiglu and residual.dtype == self.reduce_dtype:
+            from . import ops
+            if ops.residual_fusable(act, self.down):
+                y = ops.gemv_residual(act, self.down, residual)
+        if y is None:
+            y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
+            if add_here:
+                y.add_(residual)
         if self.world > 1:
             dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
         return y
