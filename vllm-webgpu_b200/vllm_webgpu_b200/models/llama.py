@@ -68,8 +68,11 @@ class LlamaB200Model(BaseB200Model):
         if residual is None:
             return self._linear(x, w, out)
         if isinstance(w, GGUFQuantTensor) and ops.residual_fusable(x, w) and out.dtype == residual.dtype:
-            ops.gemv_residual(x, w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
-            return out
+            try:
+                ops.gemv_residual(x, w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
+                return out
+            except ValueError:
+                pass  # operands the fused GEMV refuses (alignment): projection, then the add
         self._linear(x, w, out)
         out.add_(residual)
         return out

@@ -104,7 +104,10 @@ class TensorParallelSwiGLU:
         if add_here and self.fused_swiglu and residual.dtype == self.reduce_dtype:
             from . import ops
             if ops.residual_fusable(act, self.down):
-                y = ops.gemv_residual(act, self.down, residual)
+                try:
+                    y = ops.gemv_residual(act, self.down, residual)
+                except ValueError:
+                    y = None  # operands the fused GEMV refuses: projection, then the add
         if y is None:
             y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
             if add_here:
