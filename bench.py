@@ -130,72 +130,124 @@ def read_traffic(kernel_tag: str):
 # CPU baseline: the reference's quantized matmul arithmetic on host cores
 # ----------------------------------------------------------------------------
 
-def cpu_reference_rate(budget_s: float, seed: int = 0) -> dict:
-    """gguf.quants.dequantize + numpy fp32 matmul over row slabs of the layer's
-    projections, for about ``budget_s`` seconds. Returns GB/s of the same
-    algorithmic bytes (GGUF blocks + activations + outputs)."""
+_CPU_WORK = None
+
+
+def _cpu_worker_init(seed: int, max_rows: int) -> None:
+    """Per-process slabs of the seven projections (valid Q4_K blocks, finite scales)."""
+    global _CPU_WORK
+    for v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[v] = "1"  # one core per worker process
     import numpy as np
     try:
         from gguf import GGMLQuantizationType
         from gguf.quants import dequantize as deq
-        kind, how = "reference", "gguf-py 0.19 quants.dequantize + numpy fp32 matmul"
         qtype = GGMLQuantizationType.Q4_K
     except ImportError:  # the oracle port restates the same arithmetic
+        sys.path.insert(0, ROOT)
         from oracle import gguf_oracle as O
-        kind, how = "port", "oracle numpy restatement of gguf dequantize + numpy fp32 matmul"
         qtype = O.Q4_K
 
         def deq(raw, qt):
             return O.dequantize(raw, qt)
     rng = np.random.default_rng(seed)
-    slab_rows = 512
-    # per projection: a slab of random (but valid-format) Q4_K rows, x ~ N(0,1)
     work = []
-    for name, n, k in LAYER:
-        raw = rng.integers(0, 256, size=(slab_rows, k // 256 * 144), dtype=np.uint8)
-        hdr = raw.reshape(slab_rows, -1, 144)
+    for _, n, k in LAYER:
+        rows = min(n, max_rows)
+        raw = rng.integers(0, 256, size=(rows, k // 256 * 144), dtype=np.uint8)
+        hdr = raw.reshape(rows, -1, 144)
         hdr[:, :, 0:2] = np.array([1e-3], np.float16).view(np.uint8)  # finite d / dmin
         hdr[:, :, 2:4] = np.array([1e-3], np.float16).view(np.uint8)
-        x = rng.standard_normal((1, k)).astype(np.float32)
-        work.append((raw, x, slab_rows, k))
-    done_bytes = 0
-    t0 = time.perf_counter()
-    t_deq = t_mm = 0.0
-    while True:
-        for raw, x, n, k in work:
-            a = time.perf_counter()
-            w = deq(raw, qtype).reshape(n, k)
-            b = time.perf_counter()
-            _ = x @ w.T
-            c = time.perf_counter()
-            t_deq += b - a
-            t_mm += c - b
-            done_bytes += raw.nbytes + k * 2 + n * 4
-        if time.perf_counter() - t0 >= budget_s:
-            break
-    dt = time.perf_counter() - t0
-    threads = os.environ.get("OMP_NUM_THREADS") or str(os.cpu_count())
-    return {"value": done_bytes / dt / 1e9, "unit": "GB/s", "cores": int(threads), "kind": kind,
-            "sample": (f"{how}; {slab_rows}-row slabs of each of the 7 Llama-3-8B Q4_K projections, M=1, "
-                       f"{dt:.1f} s ({t_deq:.1f} s dequant, {t_mm:.1f} s matmul); BLAS threads={threads}, "
-                       f"os.cpu_count()={os.cpu_count()}")}
+        work.append((raw, rng.standard_normal((1, k)).astype(np.float32), k))
+    _CPU_WORK = (deq, qtype, work)
+
+
+def _cpu_worker_step(rows: int) -> int:
+    """Dequantize ``rows`` rows of each projection and multiply; returns the bytes."""
+    deq, qtype, work = _CPU_WORK
+    nbytes = 0
+    for raw, x, k in work:
+        r = min(rows, raw.shape[0])
+        w = deq(raw[:r], qtype).reshape(r, k)
+        _ = x @ w.T
+        nbytes += r * raw.shape[1] + r * 4
+    return nbytes
+
+
+class CpuReference:
+    """The reference's quantized-matmul arithmetic on the host cores: gguf-py's
+    ``quants.dequantize`` (the reference loader's decoder, its pinned dependency)
+    followed by a numpy fp32 matmul, over slabs of rows of the layer's seven Q4_K
+    projections at M = 1. One step = ``rows`` rows of every projection, split over
+    one worker process per host core (gguf-py's dequantize is single-threaded
+    Python + numpy). Bytes per step are the GPU arm's algorithmic bytes (GGUF
+    blocks + activations read + outputs written) for the rows processed."""
+
+    def __init__(self, seed: int = 0, max_rows: int = 2048):
+        import concurrent.futures as cf
+        import multiprocessing as mp
+        try:
+            import gguf  # noqa: F401
+            self.kind, self.how = "reference", "gguf-py 0.19 quants.dequantize + numpy fp32 matmul"
+        except ImportError:
+            self.kind, self.how = "port", "oracle numpy restatement of gguf dequantize + numpy fp32 matmul"
+        self.procs = os.cpu_count() or 1
+        self.max_rows = max_rows
+        # spawned workers: the GPU arm's process has CUDA initialised, which fork must not copy
+        self.pool = cf.ProcessPoolExecutor(self.procs, mp_context=mp.get_context("spawn"),
+                                           initializer=_cpu_worker_init, initargs=(seed, max_rows))
+        list(self.pool.map(_cpu_worker_step, [1] * self.procs))  # start every worker
+
+    def step(self, rows: int) -> int:
+        """One step over ``rows`` rows of each projection (spread over the workers); its bytes."""
+        per = max(1, -(-rows // self.procs))
+        parts = [per] * (rows // per) + ([rows % per] if rows % per else [])
+        nbytes = sum(self.pool.map(_cpu_worker_step, parts))
+        return nbytes + len(parts) * sum(k * 2 for _, _, k in LAYER)
+
+    def run(self, steps: int, warmup: int, budget_s: float) -> dict:
+        """Time ``steps`` steps after ``warmup``, each sized to about budget_s / (steps + warmup)."""
+        t = time.perf_counter()
+        self.step(8 * self.procs)
+        per_row = (time.perf_counter() - t) / (8 * self.procs)
+        target = max(0.002, min(5.0, budget_s / max(1, steps + warmup)))
+        rows = int(max(1, min(self.max_rows * self.procs, target / max(per_row, 1e-9))))
+        for _ in range(warmup):
+            self.step(rows)
+        times, nbytes = [], 0
+        for _ in range(steps):
+            t = time.perf_counter()
+            nbytes = self.step(rows)
+            times.append(time.perf_counter() - t)
+        self.pool.shutdown()
+        med = statistics.median(times)
+        return {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": self.procs, "kind": self.kind,
+                "ms_per_step": med * 1e3, "rows": rows, "bytes_per_step": nbytes,
+                "sample": (f"{self.how}; one step = {rows} rows of each of the 7 Llama-3-8B Q4_K projections, "
+                           f"M=1 ({nbytes / 1e6:.2f} MB), split over {self.procs} worker processes; median of "
+                           f"{steps} timed steps after {warmup} warm-up, {sum(times):.1f} s timed "
+                           f"(os.cpu_count()={os.cpu_count()})")}
+
+
+def cpu_reference_rate(budget_s: float, seed: int = 0) -> dict:
+    """The CPU baseline for the GPU arm's line: about ``budget_s`` seconds of steps."""
+    ref = CpuReference(seed)
+    res = ref.run(steps=10, warmup=1, budget_s=budget_s)
+    return {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
 
 def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    total_steps = args.steps + args.warmup
-    # bounded: the whole run ends within about 90 s whatever K is
-    per_step = max(0.002, min(5.0, 90.0 / max(1, total_steps)))
-    budget = per_step * args.steps
-    res = cpu_reference_rate(budget)
+    # bounded: the whole run ends within a few minutes whatever K is
+    res = CpuReference().run(args.steps, args.warmup, budget_s=90.0)
     line = {
         "metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4/u6 x fp32",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 x fp32",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
-                   "parallelism": "rank 0 only (CPU)"},
+                   "parallelism": "rank 0 only (CPU)", "rows_per_projection_per_step": res["rows"]},
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -245,28 +297,50 @@ def run_ours(args, rank: int, world: int) -> None:
         step(i % copies)
     torch.cuda.synchronize()
 
-    # one CUDA graph holding a step on each weight copy (launch overhead out of the device time)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for c in range(copies):
-            step(c)
+    # CUDA graphs of consecutive steps over the rotating weight copies (launch overhead
+    # out of the device time): a 30-step graph replayed, plus one graph for the
+    # remainder, so exactly --steps steps are timed
+    def capture(nsteps: int, first: int = 0):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for i in range(nsteps):
+                step((first + i) % copies)
+        return gr
+    chunk = 30
+    big = capture(chunk)
+    reps, rem = divmod(args.steps, chunk)
+    small = capture(rem) if rem else None
     for _ in range(3):
-        graph.replay()
+        big.replay()
     torch.cuda.synchronize()
 
-    reps = max(1, args.steps // copies)
-    steps = reps * copies
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def timed_run() -> float:
         e0.record(stream)
         for _ in range(reps):
-            graph.replay()
+            big.replay()
+        if small is not None:
+            small.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
+        return e0.elapsed_time(e1)
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = args.steps
+    # a timed region shorter than ~250 ms is repeated (same K steps each time) so the
+    # clock sampler sees it under load; the median repeat is reported
+    est = timed_run()
+    repeats = max(1, min(200, int(250.0 / max(est, 1e-3)) + 1))
+    if world > 1:
+        t = torch.tensor([repeats], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        repeats = int(t.item())
+        dist.barrier()
+    torch.cuda.synchronize()
+    runs = []
+    with ClockSampler(local) as clk:
+        for _ in range(repeats):
+            runs.append(timed_run())
+    ms = statistics.median(runs)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -293,6 +367,11 @@ def run_ours(args, rank: int, world: int) -> None:
         per[grp[0]] = e0.elapsed_time(e1) / 150
     kern_ms = sum(per.values())
     achieved = step_bytes / (kern_ms / 1e3) / 1e9
+
+    def group_bytes(idx, k) -> int:
+        return sum(LAYER[i][1] * k // 256 * 144 + m * k * 2 + m * LAYER[i][1] * 4 for i in idx) - (len(idx) - 1) * m * k * 2
+    per_frac = {nm: round(group_bytes(idx, k) / (per[nm] / 1e3) / 1e9 / float(peaks["hbm_gbs"]), 4)
+                for nm, idx, k in GROUPS}
 
     # end to end through the public model API (LlamaB200Model.layer_linears_graph: the
     # reference's per-layer projection calls, replayed from a CUDA graph as a decode
@@ -345,28 +424,94 @@ def run_ours(args, rank: int, world: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9
+    # where an end-to-end step goes: each part alone with a host wait, host wall clock
+    def host_us(fn, n=200) -> float:
+        for _ in range(5):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        return (time.perf_counter() - t0) / n * 1e6
 
-    # prefill (config 4): Q4_K GEMM M=2048, K=4096, N=14336 on the tensor cores
+    def only_h2d():
+        din.copy_(hin, non_blocking=True)
+        stream.synchronize()
+
+    def only_graph():
+        model.layer_linears_graph(0, d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], bufs)
+        stream.synchronize()
+
+    def only_d2h():
+        hout.copy_(dout, non_blocking=True)
+        stream.synchronize()
+    e2e_parts = {"h2d_and_wait_us": round(host_us(only_h2d), 2), "graph_replay_and_wait_us": round(host_us(only_graph), 2),
+                 "d2h_and_wait_us": round(host_us(only_d2h), 2), "step_us": round(e2e_ms / e2e_steps * 1e3, 2),
+                 "device_step_us": round(ms / steps * 1e3, 2)}
+
+    # prefill (config 4): Q4_K / Q6_K GEMM, K=4096, N=14336, M in {512, 2048, 8192} on the
+    # tensor cores, bf16 out; the headline key is Q4_K at M = 2048
     pre = None
+    prefill_sweep = None
     if not args.no_prefill:
-        pm, pn, pk = 2048, 14336, 4096
-        wq = layers[0][4]  # gate_proj: 14336 x 4096
-        xp = torch.randn((pm, pk), device=dev).to(torch.bfloat16)
-        yp = torch.empty((pm, pn), dtype=torch.bfloat16, device=dev)
-        for _ in range(3):
-            ops.gemm(xp, wq, out=yp)
-        torch.cuda.synchronize()
-        it = 10
-        e0.record(stream)
-        for _ in range(it):
-            ops.gemm(xp, wq, out=yp)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        pms = e0.elapsed_time(e1) / it
-        tf = 2.0 * pm * pn * pk / (pms / 1e3) / 1e12
-        pre = {"workload": "q4k_prefill_m2048_k4096_n14336", "ms": round(pms, 4), "tflops": round(tf, 2),
-               "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4),
+        pn, pk = 14336, 4096
+        wts = {Q4_K: layers[0][4], 14: random_weights(pn, pk, 14, seed=77 + rank, device=dev)}
+        prefill_sweep = {}
+        for qt, qname in ((Q4_K, "q4_k"), (14, "q6_k")):
+            for pm in (512, 2048, 8192):
+                xp = torch.randn((pm, pk), device=dev).to(torch.bfloat16)
+                yp = torch.empty((pm, pn), dtype=torch.bfloat16, device=dev)
+                for _ in range(3):
+                    ops.gemm(xp, wts[qt], out=yp)
+                torch.cuda.synchronize()
+                it = max(3, int(2e12 / (2.0 * pm * pn * pk)))  # ~10 ms of work at least
+                e0.record(stream)
+                for _ in range(it):
+                    ops.gemm(xp, wts[qt], out=yp)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                pms = e0.elapsed_time(e1) / it
+                tf = 2.0 * pm * pn * pk / (pms / 1e3) / 1e12
+                prefill_sweep[f"{qname}_m{pm}"] = {"ms": round(pms, 4), "tflops": round(tf, 2),
+                                                   "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)}
+                del xp, yp
+        p2 = prefill_sweep["q4_k_m2048"]
+        pre = {"workload": "q4k_prefill_m2048_k4096_n14336", **p2,
                "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
+        del wts
+
+    # BASELINE configs 1 and 2 on the GPU: Q8_0 4096 x 4096 matvec with fp32 x, and the
+    # Q4_0 14336 x 4096 GEMV at M in {1, 4, 8} with fp16 x; weight copies rotated past L2
+    other = None
+    if not args.no_configs:
+        other = {}
+        for key, qt, n, k, ms_, xdt, ncopy in (("config1_q8_0_matvec_f32", 8, 4096, 4096, (1,), torch.float32, 8),
+                                              ("config2_q4_0_gemv_f16", 2, 14336, 4096, (1, 4, 8), torch.float16, 5)):
+            ws_ = [random_weights(n, k, qt, seed=500 + c, device=dev) for c in range(ncopy)]
+            wb = ws_[0].nbytes
+            other[key] = {"l2": f"{ncopy} rotating weight copies ({ncopy * wb / 1e6:.0f} MB > 126 MB L2)"}
+            for mm in ms_:
+                xo = torch.randn((mm, k), generator=g, device=dev).to(xdt)
+                yo = torch.empty((mm, n), dtype=torch.float32, device=dev)
+                gr = torch.cuda.CUDAGraph()
+                for c in range(ncopy):
+                    ops.gemv(xo, ws_[c], out=yo)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(gr):
+                    for r in range(10 * ncopy):
+                        ops.gemv(xo, ws_[r % ncopy], out=yo)
+                gr.replay()
+                torch.cuda.synchronize()
+                e0.record(stream)
+                for _ in range(10):
+                    gr.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / (100 * ncopy) * 1e3
+                byts = wb + mm * k * xo.element_size() + mm * n * 4
+                other[key][f"m{mm}"] = {"us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+                                        "frac_of_hbm": round(byts / us / 1e3 / float(peaks["hbm_gbs"]), 4),
+                                        "kernel": ["stream", "f16_tc", "int8_tc"][ops.gemv_kernel(mm, ws_[0], xdt)]}
+            del ws_
 
     # batched decode of the same layer (config 3 at M = 16 and 64): the model's path above
     # M = 8 -- q/k/v and gate/up as grouped fused-dequant tcgen05 GEMMs, o and down through
@@ -451,23 +596,28 @@ def run_ours(args, rank: int, world: int) -> None:
         peak = float(peaks["hbm_gbs"])
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "timed_repeats": repeats,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 6), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "u4 x bf16 -> fp32", "data": "synthetic",
             "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
                        "projections": {nm: [k, n] for nm, n, k in LAYER},
                        "weight_bytes_per_step": sum(n * k // 256 * 144 for _, n, k in LAYER),
                        "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
-                       "graph": "CUDA graph of 3 steps", "launches_per_step": [g[0] for g in GROUPS], "parallelism": f"dp{world} (independent layer per rank)"},
+                       "graph": "CUDA graphs of 30 consecutive steps (+ one of the remainder), K steps per timed region, median of the repeated regions", "launches_per_step": [g[0] for g in GROUPS], "parallelism": f"dp{world} (independent layer per rank)"},
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": "gemv_i8_kernel<Q4_K>", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": read_traffic("gemv_q4k_layer_m1"), "peak_source": peak_src,
-                         "per_launch_us": {nm: round(v * 1e3, 2) for nm, v in per.items()}},
+                         "per_launch_us": {nm: round(v * 1e3, 2) for nm, v in per.items()},
+                         "per_launch_frac": per_frac},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "path": "LlamaB200Model.layer_linears_graph (CUDA-graph replay), one packed H2D and D2H copy from/to pinned host memory and a host wait per step"},
-            "gpu_launches": len(GROUPS) * steps,
+                    "d2h_bytes_per_step": d2h, "breakdown": e2e_parts,
+                    "path": "LlamaB200Model.layer_linears_graph (CUDA-graph replay), one packed H2D and D2H copy from/to pinned host memory and a host wait per step"},
+            "gpu_launches": len(GROUPS) * steps * repeats,
             "clocks": clocks,
             "prefill": pre,
+            "prefill_sweep": prefill_sweep,
+            "configs_1_2": other,
             "decode_batched": batched,
             "tp_ffn": tpf,
             "cpu_baseline": cpu,
@@ -485,6 +635,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-batched", action="store_true")
+    ap.add_argument("--no-configs", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))

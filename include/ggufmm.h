@@ -88,6 +88,17 @@ int ggufmm_last_cuda_error(void);
 int ggufmm_device_status(int clear, void* stream);
 
 /*
+ * Poll limit of every bounded wait on the current device (0 restores the
+ * default of 2^24 polls, seconds of waiting). A lower limit makes a wait that
+ * can never complete -- a peer GPU that never publishes its partials in
+ * ggufmm_gemv_allreduce -- give up within milliseconds; tests use it to check
+ * that such a call returns, reports the timeout through ggufmm_device_status,
+ * and leaves the context usable. Synchronous; call it between launches.
+ * No reference counterpart: the reference has no device-side waits.
+ */
+int ggufmm_set_wait_limit(uint32_t polls);
+
+/*
  * Dequantize `n_rows` rows of `k` weights: out[n, k] (row-major, out_dtype
  * F32 or F16). With out_dtype F32 the result is bit-identical to
  * gguf.quants.dequantize (gguf quants.py:241-251, 396-401, 504-522, 555-572),
@@ -101,7 +112,9 @@ int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k,
 /*
  * Decode GEMV: y[m, n] = sum_k x[m, k] * W[n, k] for 1 <= M <= 8 tokens.
  * Replaces matmul_quant.wgsl:20-61 (one thread per output row there).
- *   q       GGUF blocks [N, K/block*type_size], 16-byte aligned base
+ *   q       GGUF blocks [N, K/block*type_size], 16-byte aligned base (rows
+ *           need not be 16-byte multiples: Q6_K rows of K = 5120 / 3584 / 1536
+ *           are 4200 / 2940 / 1260 bytes)
  *   x       activations [M, K], row stride `ldx` elements (>= K), x_dtype
  *           F32 / F16 / BF16
  *   y       outputs [M, N], row stride `ldy` elements (>= N), y_dtype
@@ -159,7 +172,8 @@ int ggufmm_gemv_residual(const void* q, int qtype, int64_t n, int64_t k,
  * current device (nothing is launched): GGUFMM_GEMV_INT8 (integer tensor-core
  * GEMV, Q4_K / Q4_0), GGUFMM_GEMV_F16 (fp16 tensor-core GEMV),
  * GGUFMM_GEMV_STREAM (CUDA-core streaming GEMV, the fallback), or a negative
- * GGUFMM_ERR_* code. The reference dispatches one matmul shader per projection
+ * GGUFMM_ERR_* code (GGUFMM_ERR_ALIGN: rows that are not 16-byte multiples and
+ * too large for the fp16 GEMV's shared memory, which no decode GEMV stages). The reference dispatches one matmul shader per projection
  * whatever the shape (vllm_webgpu/models/llama.py:276-283); callers use this to
  * send shapes that only the fallback takes to ggufmm_gemm instead.
  */

@@ -49,8 +49,6 @@ def test_gemv_layer_shapes_m1(cuda, qt, n, k):
 def test_gemv_ragged_and_wide(cuda, qt, n, k, m):
     """N not a multiple of the row tile (row groups copied whole, partly filled);
     K in one piece, in several pieces, and with a short last piece."""
-    if qt == O.Q6_K and (k // 256 * 210) % 16:
-        pytest.skip("Q6_K rows of this K are not a multiple of 16 bytes (rejected with ERR_ALIGN)")
     y, ref = _run(qt, m, n, k)
     assert O.rel_err(y, ref) <= TOL
 
@@ -68,8 +66,6 @@ def test_gemv_golden_case(cuda, qt):
     from vllm_webgpu_b200 import ops
     g = golden(qt)
     m, n, k = (int(v) for v in g["mm_shape"])
-    if O.row_bytes(qt, k) % 16:
-        pytest.skip("rows not 16-byte multiples")
     y = ops.gemv(torch.from_numpy(g["mm_x"]).cuda(), _wt(g["mm_w"], qt, n, k))
     assert O.rel_err(y.cpu().numpy(), g["mm_y32"]) <= TOL
 
@@ -100,6 +96,19 @@ def test_gemv_zero_and_strided_input(cuda):
     y = ops.gemv(xs, w, out_dtype=torch.float32)
     ref = O.matmul_ref(xs.float().cpu().numpy(), raw, O.Q4_K, n, k)
     assert O.rel_err(y.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("n,k,m", [(4096, 5120, 1), (1024, 3584, 2), (4096, 1536, 1), (33, 8960, 3), (17, 2560, 8),
+                                   (64, 1280, 1)])
+def test_gemv_q6k_rows_not_16_byte_multiples(cuda, n, k, m):
+    """Q6_K rows of K/256 not a multiple of 8 (K = 5120: 4200 bytes) start at every
+    2-byte offset mod 16: staged by the fp16 tensor-core GEMV, not refused."""
+    from vllm_webgpu_b200 import ops
+    assert O.row_bytes(O.Q6_K, k) % 16
+    raw = O.make_weights(n, k, O.Q6_K, seed=5)
+    assert ops.gemv_kernel(m, _wt(raw, O.Q6_K, n, k)) == ops.GEMV_F16
+    y, ref = _run(O.Q6_K, m, n, k, seed=5)
+    assert O.rel_err(y, ref) <= TOL
 
 
 def test_gemv_no_device_timeouts(cuda):

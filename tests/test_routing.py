@@ -18,6 +18,7 @@ def _w(qt: int, n: int = 256, k: int = 4096):
     (2, 8, 0, True),     # Q4_0: the GEMV stays (no fused GEMM for it)
     (8, 8, 0, True),     # Q8_0: likewise
     (14, 3, 0, True),    # Q6_K: likewise
+    (14, 1, -3, False),  # Q6_K rows no decode GEMV can stage (ERR_ALIGN) -> GEMM
     (12, 9, 2, False),   # above the GEMV's 8 tokens
     (12, 0, 2, False),
 ])
@@ -31,8 +32,8 @@ def test_gemv_preferred_policy(monkeypatch, qt, m, kind, expect):
 
     monkeypatch.setattr(ops, "gemv_kernel", fake_kernel)
     assert ops.gemv_preferred(m, _w(qt)) is expect
-    if not 1 <= m <= ops.GEMV_MAX_M or qt != 12:
-        assert calls == []  # the device is only asked about Q4_K decode shapes
+    if not 1 <= m <= ops.GEMV_MAX_M:
+        assert calls == []  # the device is only asked about decode shapes
 
 
 def test_kernel_kind_codes_match_header():

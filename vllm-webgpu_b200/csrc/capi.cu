@@ -36,6 +36,11 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
                             int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t gemv_set_wait_limit(uint32_t polls);
+cudaError_t gemm_set_wait_limit(uint32_t polls);
+cudaError_t gemv_mma_set_wait_limit(uint32_t polls);
+cudaError_t gemm_fused_set_wait_limit(uint32_t polls);
+cudaError_t gemv_i8_set_wait_limit(uint32_t polls);
 bool gemv_i8_supported(int qtype, int64_t k, int m);
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
                                    const void* x, int xtype, int64_t m, int64_t ldx, void* const* y, int ytype,
@@ -80,6 +85,10 @@ static int cuda_status(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
   return GGUFMM_ERR_CUDA;
 }
+
+// For entry points defined in other translation units: records the CUDA error
+// (read back by ggufmm_last_cuda_error) and maps it to a status.
+int record_cuda_status(cudaError_t e) { return cuda_status(e); }
 
 static int check_device() {
   int dev = 0;
@@ -167,6 +176,16 @@ int ggufmm_device_status(int clear, void* stream) {
   return a | b | c | d | f;
 }
 
+int ggufmm_set_wait_limit(uint32_t polls) {
+  const uint32_t v = polls ? polls : (1u << 24);
+  cudaError_t e = gemv_set_wait_limit(v);
+  if (e == cudaSuccess) e = gemm_set_wait_limit(v);
+  if (e == cudaSuccess) e = gemv_mma_set_wait_limit(v);
+  if (e == cudaSuccess) e = gemm_fused_set_wait_limit(v);
+  if (e == cudaSuccess) e = gemv_i8_set_wait_limit(v);
+  return cuda_status(e);
+}
+
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
   if (!q || !out) return GGUFMM_ERR_ARG;
   if (!block_of(qtype)) return GGUFMM_ERR_QTYPE;
@@ -184,12 +203,18 @@ int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   if (s) return s;
   if (m > 8) return GGUFMM_ERR_SHAPE;
   const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
-  if (!aligned(q, 16) || row_bytes % 16 || !aligned(x, 16) || (ldx * elem_size(x_dtype)) % 16 ||
-      !aligned(y, elem_size(y_dtype)))
+  if (!aligned(q, 16) || !aligned(x, 16) || (ldx * elem_size(x_dtype)) % 16 || !aligned(y, elem_size(y_dtype)))
     return GGUFMM_ERR_ALIGN;
   if (row_bytes > 160 * 1024) return GGUFMM_ERR_SHAPE;  // one weight row must fit a shared-memory stage
   s = check_device();
   if (s) return s;
+  // Rows that are not 16-byte multiples (Q6_K with K/256 not a multiple of 8, e.g.
+  // K = 5120 / 3584 / 1536) are staged by the fp16 tensor-core GEMV only.
+  if (row_bytes % 16) {
+    if (!gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype)) return GGUFMM_ERR_ALIGN;
+    return cuda_status(launch_gemv_mma(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, row_bytes,
+                                       static_cast<cudaStream_t>(stream)));
+  }
   // integer tensor-core GEMV (Q4_K, Q4_0), else the fp16 tensor-core GEMV when the
   // shape allows (K a multiple of 256, activations fit in shared memory), else the
   // CUDA-core streaming GEMV
@@ -237,9 +262,10 @@ int ggufmm_gemv_kernel(int qtype, int64_t n, int64_t k, int64_t m, int x_dtype) 
   if (elem_size(x_dtype) == 0) return GGUFMM_ERR_DTYPE;
   const int s = check_device();
   if (s) return s;
-  if (gemv_i8_supported(qtype, k, static_cast<int>(m))) return GGUFMM_GEMV_INT8;
+  const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
+  if (row_bytes % 16 == 0 && gemv_i8_supported(qtype, k, static_cast<int>(m))) return GGUFMM_GEMV_INT8;
   if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype)) return GGUFMM_GEMV_F16;
-  return GGUFMM_GEMV_STREAM;
+  return row_bytes % 16 ? GGUFMM_ERR_ALIGN : GGUFMM_GEMV_STREAM;
 }
 
 int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k, const void* x,
@@ -403,8 +429,8 @@ int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x
   int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
   if (s) return s;
   const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
-  const bool gemv_ok = m <= 8 && aligned(q, 16) && row_bytes % 16 == 0 && row_bytes <= 160 * 1024 && aligned(x, 16) &&
-                       (ldx * elem_size(x_dtype)) % 16 == 0;
+  const bool gemv_ok = m <= 8 && aligned(q, 16) && row_bytes <= 160 * 1024 && aligned(x, 16) &&
+                       (ldx * elem_size(x_dtype)) % 16 == 0 && ggufmm_gemv_kernel(qtype, n, k, m, x_dtype) >= 0;
   // Q4_K shapes that only the streaming GEMV fits run faster on the fused-dequant GEMM,
   // when the caller passed a workspace for it
   const bool gemm_better = qtype == kQ4_K && workspace &&

@@ -54,10 +54,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 
 // ---------------------------------------------------------------------------
 // mbarrier + bulk-copy (TMA) primitives. Every wait is bounded: after
-// kWaitLimit polls the wait records kErrWaitTimeout and returns false so the
+// g_wait_limit polls (kWaitLimit unless lowered) the wait records kErrWaitTimeout and returns false so the
 // kernel can unwind instead of hanging the GPU.
 // ---------------------------------------------------------------------------
 constexpr uint32_t kWaitLimit = 1u << 24;
+
+// The poll limit in force (per translation unit, like g_device_error); the host
+// lowers it with ggufmm_set_wait_limit so a test can make a wait run out quickly.
+static __device__ uint32_t g_wait_limit = kWaitLimit;
+
+static inline cudaError_t tu_set_wait_limit(uint32_t polls) {
+  return cudaMemcpyToSymbol(g_wait_limit, &polls, sizeof(polls));
+}
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -90,7 +98,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Returns false (and flags g_device_error) if the phase never completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no limit
+  const uint32_t lim = g_wait_limit;
+  for (uint32_t i = 1; i < lim; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 256) __nanosleep(64);
   }

@@ -787,5 +787,6 @@ cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int
 }
 
 cudaError_t gemm_fused_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+cudaError_t gemm_fused_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
 }  // namespace ggufmm

@@ -312,6 +312,7 @@ static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, i
 }
 
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+cudaError_t gemm_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
 // Tensor-core GEMM on fp16 operands already in device memory:
 // w16 [n, k], x16 [m, k] (both row-major, 16-byte aligned, k % 8 == 0).

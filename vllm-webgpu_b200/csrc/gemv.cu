@@ -479,6 +479,7 @@ static cudaError_t launch_gemv_q(const GemvArgs& a, int m, int threads, int spt,
 }
 
 cudaError_t gemv_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+cudaError_t gemv_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
 // Preconditions (checked by the C-ABI): q 16-byte aligned, row_bytes % 16 == 0,
 // x 16-byte aligned with ldx*elem % 16 == 0, 1 <= m <= 8.

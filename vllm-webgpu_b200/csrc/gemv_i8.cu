@@ -116,7 +116,8 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  const uint32_t lim = g_wait_limit;
+  for (uint32_t i = 0; i < lim; ++i) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -142,7 +143,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 // bounded: gives up (error word) rather than hang when a peer never publishes
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t want) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  const uint32_t lim = g_wait_limit;
+  for (uint32_t i = 0; i < lim; ++i) {
     if (ld_acquire_sys(p) == want) return true;
     if (i > 64) __nanosleep(128);
   }
@@ -1045,5 +1047,6 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
 }
 
 cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+cudaError_t gemv_i8_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
 }  // namespace ggufmm

@@ -87,6 +87,9 @@ struct MmaArgs {
   int stages;
   int64_t nrowblocks;
   int x_pitch;      // smem bytes per column of permuted fp16 x
+  int lead;         // rows not 16-byte multiples (Q6_K, K/256 not a multiple of 8): each row's
+                    // copy starts at its 16-byte aligned-down address, the row (row_start & 15)
+                    // bytes into its smem slot
   uint32_t x_off, xsb_off, xsb_lo, red_off, bar_off;  // xsb: bf16 x-sum slots, lo part at +xsb_lo
 };
 
@@ -422,10 +425,38 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
     const int nr = static_cast<int>((sg.n - r0) < kRowsPerBlock ? (sg.n - r0) : kRowsPerBlock);
     const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
     const uint32_t bytes = static_cast<uint32_t>(units * a.unit_bytes);
-    mbar_arrive_expect_tx(&full[s], bytes * nr);
     uint8_t* dst = smem + s * a.stage_bytes;
     const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
-    for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
+    if (!a.lead) {
+      mbar_arrive_expect_tx(&full[s], bytes * nr);
+      for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
+      return;
+    }
+    // Row starts are only 2-byte aligned: copy [start & ~15, end rounded up to 16) of
+    // each row (the bytes around it belong to the neighbouring rows, inside the tensor).
+    // The tensor's very last row ends where nothing may be read beyond it: its copy
+    // stops at end & ~15 and the remaining < 16 bytes are plain loads, stored before
+    // the arrive below (whose release makes them visible with the bulk bytes).
+    const bool last_piece = r0 + nr == sg.n && ch == a.nchunks - 1;
+    uint32_t tx = 0;
+    for (int r = 0; r < nr; ++r) {
+      const uintptr_t st = reinterpret_cast<uintptr_t>(src + r * a.row_bytes), en = st + bytes;
+      const uintptr_t a0 = st & ~uintptr_t(15);
+      const uintptr_t a1 = (last_piece && r == nr - 1) ? (en & ~uintptr_t(15)) : ((en + 15) & ~uintptr_t(15));
+      tx += static_cast<uint32_t>(a1 - a0);
+      if (last_piece && r == nr - 1) {
+        uint8_t* d = dst + r * a.row_pitch + (a1 - a0);
+        for (uintptr_t o = a1; o < en; o += 2)
+          *reinterpret_cast<uint16_t*>(d + (o - a1)) = *reinterpret_cast<const uint16_t*>(o);
+      }
+    }
+    mbar_arrive_expect_tx(&full[s], tx);
+    for (int r = 0; r < nr; ++r) {
+      const uintptr_t st = reinterpret_cast<uintptr_t>(src + r * a.row_bytes), en = st + bytes;
+      const uintptr_t a0 = st & ~uintptr_t(15);
+      const uintptr_t a1 = (last_piece && r == nr - 1) ? (en & ~uintptr_t(15)) : ((en + 15) & ~uintptr_t(15));
+      bulk_g2s(dst + r * a.row_pitch, reinterpret_cast<const void*>(a0), static_cast<uint32_t>(a1 - a0), &full[s]);
+    }
   };
   __syncthreads();  // barriers initialised
   // Let the next kernel on the stream begin its own prologue as SMs free up.
@@ -549,12 +580,20 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
         }
         const int units = min(a.chunk_units, total_units - ch * a.chunk_units);
         const uint32_t sbase = static_cast<uint32_t>(s * a.stage_bytes) + g * a.row_pitch;
+        uint32_t lead_g = 0, lead_g8 = 0;  // where rows g, g+8 start inside their slots
+        if (a.lead) {
+          const int64_t rb = blockIdx.x + blk * gridDim.x;
+          const MmaSeg& sg = seg_of(a, rb);
+          const int64_t off = ((rb - sg.rb0) * kRowsPerBlock + g) * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
+          lead_g = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(sg.q) + off) & 15);
+          lead_g8 = static_cast<uint32_t>((reinterpret_cast<uintptr_t>(sg.q) + off + 8 * a.row_bytes) & 15);
+        }
         auto ctx = [&](int u) {
           const int ku = (ch * a.chunk_units + u) * kUnitK;
           UnitCtx c;
           c.smem = smem;
-          c.rg = sbase + u * a.unit_bytes;
-          c.rg8 = c.rg + 8 * a.row_pitch;
+          c.rg = sbase + lead_g + u * a.unit_bytes;
+          c.rg8 = sbase + 8 * a.row_pitch + lead_g8 + u * a.unit_bytes;
           c.xo = xcol + 2u * ku;
           c.xsh = a.xsb_off + static_cast<uint32_t>((((ku / kUnitK) * a.cols + gcol) * 4 + t) * 8);
           c.xsl_add = a.xsb_lo;
@@ -640,15 +679,18 @@ static bool plan_mma(int qt, int64_t k, int m, int xtype, int smem_budget, int W
   a.cols = xtype == GGUFMM_F32 ? 2 * m : m;
   if (a.cols > 8) return false;
   const int units = static_cast<int>(k / kUnitK);
-  // Q6_K superblocks are 210 bytes: copies stay 16-byte multiples only for 8-unit chunks
-  const int align_units = qt == kQ6_K ? 8 : 1;
-  if (units % align_units) return false;
+  // Q6_K superblocks are 210 bytes: rows are 16-byte multiples only when K/256 is a
+  // multiple of 8; otherwise every row's copy starts at its aligned-down address
+  // (a.lead) and its slot holds up to 15 bytes more. Chunks of 8 / 16 units stay
+  // 16-byte multiples, so only the row start moves.
+  a.lead = qt == kQ6_K && units % 8 != 0;
   a.chunk_units = std::min(units, kMaxChunkUnits);
-  a.chunk_units -= a.chunk_units % align_units;
+  if (qt == kQ6_K && a.chunk_units >= 8) a.chunk_units -= a.chunk_units % 8;
   a.nchunks = (units + a.chunk_units - 1) / a.chunk_units;
   a.chunk_bytes = a.chunk_units * a.unit_bytes;
-  if (a.chunk_bytes % 16) return false;
-  a.row_pitch = (a.chunk_bytes + 127) / 128 * 128 + 32;  // pitch = 32 mod 128: conflict-free 8-byte row reads
+  if (a.chunk_bytes % 16 && !(a.lead && a.nchunks == 1)) return false;
+  // pitch = 32 mod 128: conflict-free 8-byte row reads (+16 for the aligned-down start)
+  a.row_pitch = (a.chunk_bytes + (a.lead ? 16 : 0) + 127) / 128 * 128 + 32;
   a.stage_bytes = kRowsPerBlock * a.row_pitch;
   a.x_pitch = static_cast<int>(2 * k + 64);
   const int x_bytes = a.cols * a.x_pitch;
@@ -757,5 +799,6 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
 }
 
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+cudaError_t gemv_mma_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
 }  // namespace ggufmm

@@ -37,6 +37,7 @@ cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, 
                               cudaStream_t st);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
                             int64_t ldy, cudaStream_t st);
+int record_cuda_status(cudaError_t e);  // capi.cu: keeps the code for ggufmm_last_cuda_error
 
 // The library-owned scratch. In host code this name is only a stand-in for the
 // symbol, not a device address; the address comes from cudaGetSymbolAddress.
@@ -91,17 +92,18 @@ extern "C" int ggufmm_gemm_noalloc(const void* q, int qtype, int64_t n, int64_t 
       (reinterpret_cast<uintptr_t>(y) & (ys - 1)))
     return GGUFMM_ERR_ALIGN;
   int dev = 0, major = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-    return GGUFMM_ERR_CUDA;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e != cudaSuccess) return record_cuda_status(e);
   if (major != 10) return GGUFMM_ERR_DEVICE;
   void* scratch = nullptr;
-  if (scratch_address(&scratch) != cudaSuccess) return GGUFMM_ERR_CUDA;
+  e = scratch_address(&scratch);
+  if (e != cudaSuccess) return record_cuda_status(e);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* w16 = static_cast<uint8_t*>(scratch);
   uint8_t* x16 = w16 + w_bytes;
-  cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
+  e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
   if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
   if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st);
-  return e == cudaSuccess ? GGUFMM_OK : GGUFMM_ERR_CUDA;
+  return record_cuda_status(e);
 }

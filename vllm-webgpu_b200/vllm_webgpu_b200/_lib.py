@@ -37,6 +37,7 @@ SIGNATURES = {
     "ggufmm_status_string": (ctypes.c_char_p, [_I]),
     "ggufmm_last_cuda_error": (_I, []),
     "ggufmm_device_status": (_I, [_I, _VP]),
+    "ggufmm_set_wait_limit": (_I, [ctypes.c_uint32]),
     "ggufmm_dequantize": (_I, [_VP, _I, _I64, _I64, _VP, _I, _VP]),
     "ggufmm_gemv": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
     "ggufmm_gemv_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP]),
@@ -86,6 +87,21 @@ class GGUFMMError(RuntimeError):
     """A CUDA-side failure reported by libggufmm."""
 
 
+class GGUFMMValueError(ValueError):
+    """An argument the library refused before launching anything; ``status`` is
+    the GGUFMM_ERR_* code (so callers can tell an alignment refusal, which a
+    slower path may serve, from a caller-side shape or dtype bug)."""
+
+    def __init__(self, msg: str, status: int):
+        super().__init__(msg)
+        self.status = status
+
+
+def is_align_refusal(exc: BaseException) -> bool:
+    """True when ``exc`` is the library's refusal of misaligned operands."""
+    return isinstance(exc, GGUFMMValueError) and exc.status == ERR_ALIGN
+
+
 def check(status: int, what: str) -> None:
     """Map a status code to the exception the reference would raise.
 
@@ -100,4 +116,4 @@ def check(status: int, what: str) -> None:
         raise GGUFMMError(f"{what}: {msg} (cudaError {lib().ggufmm_last_cuda_error()})")
     if status == ERR_DEVICE:
         raise GGUFMMError(f"{what}: {msg}")
-    raise ValueError(f"{what}: {msg} (status {status})")
+    raise GGUFMMValueError(f"{what}: {msg} (status {status})", status)

@@ -93,9 +93,10 @@ class BaseB200Model:
             raise ValueError("matmul_quant: USE_QUANT=1 needs a GGUFQuantTensor weight")
         if tuple(w.shape) != (n, k):
             raise ValueError(f"matmul_quant: weight is {tuple(w.shape)}, constants say N={n}, K={k}")
-        torch.matmul(x.reshape(-1, k).to(w.dtype), w.t(), out=None if out.dtype != w.dtype else out.reshape(-1, n))
-        if out.dtype != w.dtype:
-            out.reshape(-1, n).copy_(torch.matmul(x.reshape(-1, k).to(w.dtype), w.t()))
+        y = torch.matmul(x.reshape(-1, k).to(w.dtype), w.t())
+        # copy_ writes into `out` whatever its strides (out.reshape of a non-contiguous
+        # tensor would be a temporary copy, and the result would be lost)
+        out.copy_(y.reshape(out.shape))
 
     def forward(self, input_ids, positions, attn_metadata):  # pragma: no cover - out of scope
         raise NotImplementedError("attention / norm / rope are outside the quantized-matmul path")

@@ -14,7 +14,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import ops
+from .. import _lib, ops
 from ..formats import GGUFQuantTensor
 from .base import BaseB200Model
 
@@ -23,6 +23,16 @@ PROJ = {
     "o": "self_attn.o_proj.weight", "gate": "mlp.gate_proj.weight", "up": "mlp.up_proj.weight",
     "down": "mlp.down_proj.weight",
 }
+
+
+def _overlaps(a: torch.Tensor, b: torch.Tensor) -> bool:
+    """Whether two tensors share any bytes of storage."""
+    if a.device != b.device or a.untyped_storage().data_ptr() != b.untyped_storage().data_ptr():
+        return False
+    a0, b0 = a.data_ptr(), b.data_ptr()
+    a1 = a0 + (a.numel() and (sum((s - 1) * st for s, st in zip(a.shape, a.stride())) + 1) * a.element_size())
+    b1 = b0 + (b.numel() and (sum((s - 1) * st for s, st in zip(b.shape, b.stride())) + 1) * b.element_size())
+    return a0 < b1 and b0 < a1
 
 
 class LlamaB200Model(BaseB200Model):
@@ -71,8 +81,16 @@ class LlamaB200Model(BaseB200Model):
             try:
                 ops.gemv_residual(x, w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
                 return out
-            except ValueError:
-                pass  # operands the fused GEMV refuses (alignment): projection, then the add
+            except ValueError as exc:
+                if not _lib.is_align_refusal(exc):
+                    raise
+                # misaligned operands, which the fused GEMV refuses: projection, then the add
+        if out.data_ptr() == residual.data_ptr() or _overlaps(out, residual):
+            # h = h + proj in place: project into a temporary so the residual survives
+            tmp = torch.empty_like(out)
+            self._linear(x, w, tmp)
+            torch.add(tmp, residual, out=out)
+            return out
         self._linear(x, w, out)
         out.add_(residual)
         return out
@@ -100,8 +118,10 @@ class LlamaB200Model(BaseB200Model):
                 and ops.swiglu_fusable(ffn_normed, gate, up)):
             try:
                 return ops.gemv_swiglu(ffn_normed, gate, up, out=act_buf.reshape(-1, gate.n))
-            except ValueError:
-                pass  # activations too large for the fused kernel's shared memory
+            except ValueError as exc:
+                if not _lib.is_align_refusal(exc):
+                    raise
+                # misaligned operands: the two projections and the activation separately
         g = torch.empty_like(act_buf, dtype=torch.float32)
         u = torch.empty_like(act_buf, dtype=torch.float32)
         self.project_gate_up(layer, ffn_normed, g, u)

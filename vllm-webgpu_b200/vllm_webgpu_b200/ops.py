@@ -95,14 +95,16 @@ _gemv_kernels: dict = {}
 
 def gemv_kernel(m: int, w: GGUFQuantTensor, x_dtype: torch.dtype = torch.bfloat16) -> int:
     """Which decode GEMV kernel ``gemv`` launches for M tokens against ``w`` on the
-    weight's device: GEMV_INT8, GEMV_F16 or GEMV_STREAM (the CUDA-core fallback)."""
+    weight's device: GEMV_INT8, GEMV_F16 or GEMV_STREAM (the CUDA-core fallback), or
+    ``_lib.ERR_ALIGN`` when no decode GEMV can stage the weight's rows."""
     dev = _require_cuda(w.data)
     key = (dev.index, w.qtype, w.n, w.k, m, x_dtype)
     kind = _gemv_kernels.get(key)
     if kind is None:
         with torch.cuda.device(dev):
             kind = int(_lib.lib().ggufmm_gemv_kernel(w.qtype, w.n, w.k, m, _code(x_dtype)))
-        _lib.check(min(kind, 0), "ggufmm_gemv_kernel")
+        if kind != _lib.ERR_ALIGN:  # ERR_ALIGN: no decode GEMV can stage these rows
+            _lib.check(min(kind, 0), "ggufmm_gemv_kernel")
         _gemv_kernels[key] = kind
     return kind
 
@@ -114,7 +116,8 @@ def gemv_preferred(m: int, w: GGUFQuantTensor, x_dtype: torch.dtype = torch.bflo
     is 2-4x faster)."""
     if not 1 <= m <= GEMV_MAX_M:
         return False
-    return w.qtype != 12 or gemv_kernel(m, w, x_dtype) != GEMV_STREAM
+    kind = gemv_kernel(m, w, x_dtype)
+    return kind >= 0 and (w.qtype != 12 or kind != GEMV_STREAM)
 
 
 def gemv_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Tensor] | None = None,
@@ -147,10 +150,12 @@ def gemv_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Te
 
 
 def swiglu_fusable(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor) -> bool:
-    """Whether gemv_swiglu handles these operands (decode M, Q4_K / Q4_0, K % 256 == 0)."""
+    """Whether gemv_swiglu handles these operands (decode M, Q4_K / Q4_0, K % 256 == 0,
+    and the activations fit the integer GEMV's shared memory)."""
     m = x.numel() // max(x.shape[-1], 1)
-    return (1 <= m <= GEMV_MAX_M and gate.qtype == up.qtype and gate.qtype in (2, 12) and gate.shape == up.shape
-            and gate.k % 256 == 0 and x.shape[-1] == gate.k)
+    return (x.is_cuda and 1 <= m <= GEMV_MAX_M and gate.qtype == up.qtype and gate.qtype in (2, 12)
+            and gate.shape == up.shape and gate.k % 256 == 0 and x.shape[-1] == gate.k
+            and gemv_kernel(m, gate, x.dtype) == GEMV_INT8)
 
 
 def gemv_swiglu(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor, out: torch.Tensor | None = None,
@@ -326,8 +331,10 @@ def mul_mat(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None
     if x2.is_cuda and gemv_preferred(m, w, x2.dtype):
         try:
             y = gemv(x2, w, out=out, out_dtype=out_dtype)
-        except ValueError:
-            # unaligned operands: the GEMM path has no alignment requirement
+        except ValueError as exc:
+            if not _lib.is_align_refusal(exc):
+                raise
+            # unaligned operands: the GEMM path has no 16-byte alignment requirement
             y = gemm(x2, w, out=out, out_dtype=out_dtype)
     else:
         y = gemm(x2, w, out=out, out_dtype=out_dtype)

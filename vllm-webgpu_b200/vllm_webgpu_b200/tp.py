@@ -26,6 +26,7 @@ from typing import Callable
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .formats import QUANT_SIZES, GGUFQuantTensor
 
 
@@ -86,10 +87,12 @@ class TensorParallelSwiGLU:
             from . import ops
             if ops.swiglu_fusable(x, self.gate, self.up):
                 # decode: gate, up and SwiGLU in one launch (fp32 activation); shapes whose
-                # activations do not fit the kernel's shared memory take the unfused path
+                # activations do not fit the kernel's shared memory are excluded by swiglu_fusable
                 try:
                     act = ops.gemv_swiglu(x, self.gate, self.up, out_dtype=torch.float32)
-                except ValueError:
+                except ValueError as exc:
+                    if not _lib.is_align_refusal(exc):
+                        raise
                     act = None
         if act is None:
             g = self.matmul(x, self.gate, out_dtype=torch.float32)
@@ -106,8 +109,10 @@ class TensorParallelSwiGLU:
             if ops.residual_fusable(act, self.down):
                 try:
                     y = ops.gemv_residual(act, self.down, residual)
-                except ValueError:
-                    y = None  # operands the fused GEMV refuses: projection, then the add
+                except ValueError as exc:
+                    if not _lib.is_align_refusal(exc):
+                        raise
+                    y = None  # misaligned operands the fused GEMV refuses: projection, then the add
         if y is None:
             y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
             if add_here:
