@@ -11,7 +11,7 @@ against the oracle (gguf-py's dequantize restated in numpy, then a float64 matmu
    M in {1, 32, 2048}; sampled tokens and output features against the oracle FFN.
 
 Gates: max|y - y_ref| / rms(y_ref) <= 2e-3 for fp32 outputs. A bf16 output adds its
-own rounding, half a bf16 ulp of |y_ref| (2^-9 relative) per element. The FFN is a
+own rounding, half a bf16 ulp of |y_ref| (at most 2^-8 relative) per element. The FFN is a
 chain of three matmuls with an fp32 SwiGLU between them, so its gate is 1.5 x 2e-3.
 """
 from __future__ import annotations
@@ -25,7 +25,7 @@ from tests.helpers import TOL
 
 pytestmark = pytest.mark.gpu
 
-BF16_HALF_ULP = 2.0 ** -9
+BF16_HALF_ULP = 2.0 ** -8  # half a bf16 ulp, relative to the value (worst case at a binade bottom)
 
 
 def _wt(raw: np.ndarray, qt: int, n: int, k: int):

@@ -48,3 +48,42 @@ def test_layer_linears_match_oracle(cuda, graph, m):
         for p, (n, k) in SHAPES.items():
             ref = O.matmul_ref(xs[INPUT[p]].float().cpu().numpy(), raws[p], O.Q4_K, n, k)
             assert O.rel_err(bufs[p].cpu().numpy(), ref) <= TOL, (p, rep)
+
+
+@pytest.mark.parametrize("m", [1, 16])
+def test_layer_linears_graph_with_staged_host_copies(cuda, m):
+    """The serving path: one replay copies the activations in from pinned host memory,
+    runs the projections and copies the outputs back; the host buffers are refilled
+    between replays."""
+    model, raws = _model(cuda)
+    dims = (("normed", 512), ("attn_out", 512), ("ffn_normed", 512), ("ffn_act", 1792))
+    kin = sum(k for _, k in dims)
+    hin = torch.empty((m, kin), dtype=torch.bfloat16).pin_memory()
+    din = torch.empty((m, kin), dtype=torch.bfloat16, device="cuda")
+    xs, off = {}, 0
+    for nm, k in dims:
+        xs[nm] = din[:, off:off + k]
+        off += k
+    nout = sum(n for n, _ in SHAPES.values())
+    dout = torch.empty((m * nout,), dtype=torch.float32, device="cuda")
+    hout = torch.empty_like(dout, device="cpu").pin_memory()
+    bufs, off = {}, 0
+    for p, (n, _) in SHAPES.items():
+        bufs[p] = dout[off:off + m * n].view(m, n)
+        off += m * n
+    for rep in range(3):
+        hin.copy_(torch.from_numpy(O.make_activations(m, kin, seed=90 + rep)).to(torch.bfloat16))
+        model.layer_linears_graph(0, xs["normed"], xs["attn_out"], xs["ffn_normed"], xs["ffn_act"], bufs,
+                                  stage_in=[(din, hin)], stage_out=[(hout, dout)])
+        torch.cuda.current_stream().synchronize()
+        off = 0
+        hx = {}
+        for nm, k in dims:
+            hx[nm] = hin[:, off:off + k].float().numpy()
+            off += k
+        off = 0
+        for p, (n, k) in SHAPES.items():
+            got = hout[off:off + m * n].view(m, n).numpy()
+            off += m * n
+            ref = O.matmul_ref(hx[INPUT[p]], raws[p], O.Q4_K, n, k)
+            assert O.rel_err(got, ref) <= TOL, (p, rep)

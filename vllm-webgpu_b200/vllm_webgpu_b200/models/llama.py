@@ -143,25 +143,44 @@ class LlamaB200Model(BaseB200Model):
         self.project_down(layer, ffn_act, bufs["down"])
         return bufs
 
-    def layer_linears_graph(self, layer: int, normed, attn_out, ffn_normed, ffn_act, bufs: dict) -> dict:
+    def layer_linears_graph(self, layer: int, normed, attn_out, ffn_normed, ffn_act, bufs: dict,
+                            stage_in: list | None = None, stage_out: list | None = None) -> dict:
         """``layer_linears`` replayed from a CUDA graph, the decode serving path:
         the launches are captured once per (layer, buffer addresses) and then
         replayed with one host call. The inputs and ``bufs`` must be the same
         tensors (static buffers the caller refills) on every call; the replay is
-        ordered on the current stream."""
+        ordered on the current stream.
+
+        ``stage_in`` / ``stage_out``: optional (destination, source) pairs of
+        host <-> device copies captured into the same graph, before and after the
+        projections -- pinned host buffers the caller refills / reads, so one
+        replay moves a decode step's activations in and its outputs out."""
+        stage_in, stage_out = list(stage_in or ()), list(stage_out or ())
+        for dst, src in stage_in + stage_out:
+            host = src if src.device.type == "cpu" else dst
+            if not host.is_pinned():
+                raise ValueError("staged host buffers must be pinned")
         key = (layer, normed.data_ptr(), attn_out.data_ptr(), ffn_normed.data_ptr(), ffn_act.data_ptr(),
-               tuple((k, b.data_ptr()) for k, b in sorted(bufs.items())))
+               tuple((k, b.data_ptr()) for k, b in sorted(bufs.items())),
+               tuple((d.data_ptr(), s.data_ptr()) for d, s in stage_in + stage_out))
         graphs = self.__dict__.setdefault("_layer_graphs", {})
         g = graphs.get(key)
         cur = torch.cuda.current_stream(self.device)
+
+        def body():
+            for dst, src in stage_in:
+                dst.copy_(src, non_blocking=True)
+            self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)
+            for dst, src in stage_out:
+                dst.copy_(src, non_blocking=True)
         if g is None:
             side = torch.cuda.Stream(self.device)
             side.wait_stream(cur)
             with torch.cuda.stream(side):
-                self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)  # warm-up
+                body()  # warm-up
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=side):
-                self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)
+                body()
             cur.wait_stream(side)
             graphs[key] = g
         g.replay()
