@@ -81,8 +81,9 @@ int ggufmm_last_cuda_error(void);
 
 /*
  * Device-side status word: every spin-wait inside the kernels is bounded and,
- * when it gives up, ORs 1 into this word and unwinds instead of hanging.
- * Returns the word (>= 0; 0 = no timeout seen) or a negative status.
+ * when it gives up, ORs 1 into this word and unwinds instead of hanging; an
+ * embedding id out of range ORs 2. Returns the word (>= 0; 0 = nothing seen)
+ * or a negative status.
  * Synchronizes `stream`; clears the word when `clear` is nonzero.
  */
 int ggufmm_device_status(int clear, void* stream);
@@ -108,6 +109,22 @@ int ggufmm_set_wait_limit(uint32_t polls);
  */
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k,
                       void* out, int out_dtype, void* stream);
+
+/*
+ * Quantized embedding lookup: out[t, :] = dequantize(row ids[t] of the table) for
+ * t < n_ids. Replaces the reference's embedding_lookup dispatch
+ * (vllm_webgpu/models/llama.py:170-178, shaders/generic/embedding_lookup.wgsl),
+ * which copied rows of an f16 table; here the table stays in its GGUF blocks
+ * (token_embd.weight, [n_vocab, k/block*type_size]). out_dtype F32 is
+ * bit-identical to gguf.quants.dequantize of the row; F16 / BF16 round that value
+ * once. ids are int32 (the reference's u32 token ids below 2^31). An id outside
+ * [0, n_vocab) gives a zero row and sets bit 2 of the device status word
+ * (ggufmm_device_status). q needs 2-byte alignment, out 16-byte alignment and a
+ * row stride ldo (elements, >= k) whose bytes are a multiple of 16.
+ */
+int ggufmm_embedding(const void* q, int qtype, int64_t n_vocab, int64_t k,
+                     const int32_t* ids, int64_t n_ids,
+                     void* out, int out_dtype, int64_t ldo, void* stream);
 
 /*
  * Decode GEMV: y[m, n] = sum_k x[m, k] * W[n, k] for 1 <= M <= 8 tokens.

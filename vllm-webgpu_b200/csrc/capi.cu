@@ -36,6 +36,9 @@ cudaError_t launch_gemv_mma(const void* q, int qtype, int64_t n, int64_t k, cons
                             int64_t ldx, void* y, int ytype, int64_t ldy, int64_t row_bytes, cudaStream_t st);
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t dequant_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t launch_embedding(const void* q, int qtype, int64_t n_vocab, int64_t k, const int32_t* ids, int64_t n_ids,
+                             void* out, int out_dtype, int64_t ldo, cudaStream_t st);
 cudaError_t gemv_set_wait_limit(uint32_t polls);
 cudaError_t gemm_set_wait_limit(uint32_t polls);
 cudaError_t gemv_mma_set_wait_limit(uint32_t polls);
@@ -166,14 +169,15 @@ const char* ggufmm_status_string(int s) {
 
 int ggufmm_device_status(int clear, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int a = 0, b = 0, c = 0, d = 0, f = 0;
+  int a = 0, b = 0, c = 0, d = 0, f = 0, h = 0;
   cudaError_t e = gemv_device_error(&a, clear, st);
   if (e == cudaSuccess) e = gemm_device_error(&b, clear, st);
   if (e == cudaSuccess) e = gemv_mma_device_error(&c, clear, st);
   if (e == cudaSuccess) e = gemm_fused_device_error(&d, clear, st);
   if (e == cudaSuccess) e = gemv_i8_device_error(&f, clear, st);
+  if (e == cudaSuccess) e = dequant_device_error(&h, clear, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return a | b | c | d | f;
+  return a | b | c | d | f | h;
 }
 
 int ggufmm_set_wait_limit(uint32_t polls) {
@@ -195,6 +199,22 @@ int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void*
   int s = check_device();
   if (s) return s;
   return cuda_status(launch_dequant(q, qtype, n_rows, k, out, out_dtype, static_cast<cudaStream_t>(stream)));
+}
+
+int ggufmm_embedding(const void* q, int qtype, int64_t n_vocab, int64_t k, const int32_t* ids, int64_t n_ids,
+                     void* out, int out_dtype, int64_t ldo, void* stream) {
+  if (!q || !ids || !out) return GGUFMM_ERR_ARG;
+  if (!block_of(qtype)) return GGUFMM_ERR_QTYPE;
+  if (!elem_size(out_dtype)) return GGUFMM_ERR_DTYPE;
+  if (n_vocab <= 0 || n_ids <= 0 || k <= 0 || k % block_of(qtype) || k > kMaxK || ldo < k ||
+      n_ids > (int64_t(1) << 31) - 1)
+    return GGUFMM_ERR_SHAPE;
+  if (!aligned(q, 2) || !aligned(ids, 4) || !aligned(out, 16) || (ldo * elem_size(out_dtype)) % 16)
+    return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  return cuda_status(launch_embedding(q, qtype, n_vocab, k, ids, n_ids, out, out_dtype, ldo,
+                                      static_cast<cudaStream_t>(stream)));
 }
 
 int ggufmm_gemv(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, int64_t ldx,

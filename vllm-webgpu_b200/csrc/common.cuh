@@ -117,6 +117,25 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// L2 policy for data read exactly once per call (the weight stream of a GEMV):
+// evict first, so the stream does not push the small, reused activations and
+// outputs out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s with an L2 cache policy (from createpolicy).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Activation loads: 16 consecutive elements of x (f32 / f16 / bf16) -> fp32.
 // The caller guarantees 16-byte alignment of the first element.

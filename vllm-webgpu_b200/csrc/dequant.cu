@@ -225,6 +225,97 @@ cudaError_t launch_dequant(const void* q, int qtype, int64_t n_rows, int64_t k, 
 #undef GGUFMM_DQ
 }
 
+// ---- quantized embedding lookup ------------------------------------------------------
+// out[t, :] = dequantize(table row ids[t]) for t < n_ids: the reference's
+// embedding_lookup shader (vllm_webgpu/shaders/generic/embedding_lookup.wgsl, one
+// workgroup per token copying an f16 row), on the GGUF blocks of the table itself
+// (token_embd is usually Q4_K / Q6_K in a GGUF file). One thread per 32 outputs, the
+// same bit-exact decode as dequant_kernel; fp32 output is gguf's value, f16 / bf16 its
+// single rounding. An id outside [0, n_vocab) writes a zero row and sets
+// kErrIndex in the device status word (the reference does not check).
+constexpr int kErrIndex = 2;
+
+template <int OT>
+__device__ __forceinline__ void store32(void* out, const float* v) {
+  uint4* o = reinterpret_cast<uint4*>(out);
+  if (OT == GGUFMM_F32) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      o[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
+                        __float_as_uint(v[4 * i + 3]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t h[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = v[8 * i + 2 * j], b = v[8 * i + 2 * j + 1];
+        if (OT == GGUFMM_F16) {
+          __half2 h2 = __floats2half2_rn(a, b);
+          h[j] = *reinterpret_cast<uint32_t*>(&h2);
+        } else {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+          h[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+      }
+      o[i] = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+  }
+}
+
+template <int QT, int OT>
+__global__ void __launch_bounds__(256) embed_kernel(const uint8_t* __restrict__ q, int64_t n_vocab, int64_t row_bytes,
+                                                    int units_per_row, const int32_t* __restrict__ ids, int64_t n_ids,
+                                                    void* __restrict__ out, int64_t ldo) {
+  const int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (u >= n_ids * units_per_row) return;
+  const int64_t t = u / units_per_row;
+  const int c = static_cast<int>(u - t * units_per_row);
+  const int64_t id = __ldg(ids + t);
+  float v[32];
+  if (id >= 0 && id < n_vocab) {
+    dequant32<QT>(q + id * row_bytes, c, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    if (c == 0) atomicOr(&g_device_error, kErrIndex);
+  }
+  constexpr int es = OT == GGUFMM_F32 ? 4 : 2;
+  store32<OT>(static_cast<uint8_t*>(out) + (t * ldo + 32 * c) * es, v);
+}
+
+template <int QT, int OT>
+static cudaError_t launch_embed_t(const void* q, int64_t n_vocab, int64_t k, const int32_t* ids, int64_t n_ids,
+                                  void* out, int64_t ldo, cudaStream_t st) {
+  const int units_per_row = static_cast<int>(k / 32);
+  const int64_t n_units = n_ids * units_per_row;
+  const int64_t row_bytes = k / QTraits<QT>::kBlock * QTraits<QT>::kBytes;
+  const int threads = 256;
+  embed_kernel<QT, OT><<<static_cast<unsigned>((n_units + threads - 1) / threads), threads, 0, st>>>(
+      static_cast<const uint8_t*>(q), n_vocab, row_bytes, units_per_row, ids, n_ids, out, ldo);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embedding(const void* q, int qtype, int64_t n_vocab, int64_t k, const int32_t* ids, int64_t n_ids,
+                             void* out, int out_dtype, int64_t ldo, cudaStream_t st) {
+#define GGUFMM_EMB(QT)                                                                                   \
+  case QT:                                                                                               \
+    return out_dtype == GGUFMM_F32   ? launch_embed_t<QT, GGUFMM_F32>(q, n_vocab, k, ids, n_ids, out, ldo, st) \
+           : out_dtype == GGUFMM_F16 ? launch_embed_t<QT, GGUFMM_F16>(q, n_vocab, k, ids, n_ids, out, ldo, st) \
+                                     : launch_embed_t<QT, GGUFMM_BF16>(q, n_vocab, k, ids, n_ids, out, ldo, st);
+  switch (qtype) {
+    GGUFMM_EMB(kQ4_0)
+    GGUFMM_EMB(kQ8_0)
+    GGUFMM_EMB(kQ4_K)
+    GGUFMM_EMB(kQ6_K)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef GGUFMM_EMB
+}
+
+cudaError_t dequant_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
+
 // Activation cast x[M, K] (row stride ldx, f32/f16/bf16) -> fp16 [M, K]
 // contiguous, 8 elements per thread. bf16 -> fp16 is exact for |x| in the
 // fp16 normal range; values beyond +-65504 become +-inf.

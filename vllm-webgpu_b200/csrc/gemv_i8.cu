@@ -371,8 +371,9 @@ __device__ __forceinline__ const Seg& block_rows(const I8Args& a, int64_t lb, in
 __device__ __forceinline__ int q40_pos(int e) { return e < 16 ? (e >> 2) * 8 + (e & 3) : ((e - 16) >> 2) * 8 + 4 + (e & 3); }
 
 // EXT: the SwiGLU / all-reduce epilogue variants (plain GEMVs compile without them)
-template <int QT, int NCG, int NCC, int W, bool EXT>
-__global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(const I8Args a) {
+// MINB: CTAs per SM the launch is shaped for (registers are capped to fit them).
+template <int QT, int NCG, int NCC, int W, bool EXT, int MINB>
+__global__ void __launch_bounds__((W + 2) * 32, MINB) gemv_i8_kernel(const I8Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.bar_off);
@@ -410,6 +411,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     fence_mbar_init();
   }
 
+  const uint64_t wpol = l2_evict_first_policy();  // weights are read once per call
   auto issue = [&](int64_t p, int s) {
     const int64_t rb = block_of<EXT>(a, cid, ncl, p / a.nchunks);
     const int ch = static_cast<int>(p % a.nchunks);
@@ -425,7 +427,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     // rg > 1 only when a chunk is the whole row (one chunk, no K split): rg consecutive rows are contiguous
     for (int r = 0, grp = 0; r < nr; r += a.rg, ++grp) {
       const uint32_t rows = static_cast<uint32_t>(min(a.rg, nr - r));
-      bulk_g2s(dst + grp * a.group_pitch, src + r * a.row_bytes, rows * bytes, &full[s]);
+      bulk_g2s_hint(dst + grp * a.group_pitch, src + r * a.row_bytes, rows * bytes, &full[s], wpol);
     }
   };
 
@@ -452,7 +454,7 @@ __global__ void __launch_bounds__((W + 2) * 32, W <= 4 ? 2 : 1) gemv_i8_kernel(c
     // ---- activations -> digits. One warp per (token, unit): lane l holds x[8l..8l+7].
     // kB tasks of a warp go through each step together (step-major, straight-line
     // code), so their load round trips and reduction chains overlap.
-    constexpr int kStagers = W + 1, kB = W == 8 ? 8 : 4;
+    constexpr int kStagers = W + 1, kB = W == 8 && MINB == 1 ? 8 : 4;
     const int ntask = a.m * units;
     for (int base = warp < W ? warp : W; base < ntask; base += kB * kStagers) {
       int tok[kB], un[kB];
@@ -864,10 +866,10 @@ bool plan_i8(int qt, int64_t k, int m, int smem_budget, int W, int ksplit, I8Arg
 std::mutex g_attr_mu;
 std::set<std::pair<const void*, int>> g_attr_done;
 
-template <int QT, int NCG, int W, bool EXT>
+template <int QT, int NCG, int W, bool EXT, int MINB>
 cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   constexpr int NCC = NCG == 1 ? 1 : 2;
-  auto fn = gemv_i8_kernel<QT, NCG, NCC, W, EXT>;
+  auto fn = gemv_i8_kernel<QT, NCG, NCC, W, EXT, MINB>;
   const int smem = static_cast<int>(a.bar_off + 8 * (2 * a.stages + 2 * kRedBufs + 4));
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
@@ -895,52 +897,64 @@ cudaError_t launch_t(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t s
   return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
-template <int QT, int W>
+template <int QT, int W, int MINB>
 cudaError_t launch_q(I8Args& a, int dev, int sms, int smem_optin, cudaStream_t st) {
   const bool ext = a.swiglu || a.tp_world > 1 || a.resid;
   switch (ncg_of(a.m)) {
-    case 1: return ext ? launch_t<QT, 1, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 1, W, false>(a, dev, sms, smem_optin, st);
-    case 2: return ext ? launch_t<QT, 2, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 2, W, false>(a, dev, sms, smem_optin, st);
-    default: return ext ? launch_t<QT, 3, W, true>(a, dev, sms, smem_optin, st) : launch_t<QT, 3, W, false>(a, dev, sms, smem_optin, st);
+    case 1: return ext ? launch_t<QT, 1, W, true, MINB>(a, dev, sms, smem_optin, st) : launch_t<QT, 1, W, false, MINB>(a, dev, sms, smem_optin, st);
+    case 2: return ext ? launch_t<QT, 2, W, true, MINB>(a, dev, sms, smem_optin, st) : launch_t<QT, 2, W, false, MINB>(a, dev, sms, smem_optin, st);
+    default: return ext ? launch_t<QT, 3, W, true, MINB>(a, dev, sms, smem_optin, st) : launch_t<QT, 3, W, false, MINB>(a, dev, sms, smem_optin, st);
   }
 }
 
 // CTA shape: 4 compute warps in <= 113 KB of shared memory, two CTAs per SM
 // (the next launch's CTAs become resident, and start streaming their weights,
 // as soon as any CTA of the previous one exits), when the activations and two
-// ring stages fit; else 8 compute warps, one CTA per SM. GGUFMM_GEMV_WARPS=8 or
-// 16 forces the one-CTA shape (tuning).
+// ring stages fit; else 8 compute warps, one CTA per SM. GGUFMM_GEMV_WARPS=8
+// forces the one-CTA shape (tuning).
 int forced_warps() {
   static const int w = [] {
     const char* e = std::getenv("GGUFMM_GEMV_WARPS");
     const int v = e ? std::atoi(e) : 0;
-    return v == 16 || v == 8 ? v : 0;
+    return v == 8 ? v : 0;
   }();
   return w;
 }
-// GGUFMM_GEMV_KSPLIT=0: never split K; =1: split K whenever the 4-warp shape
-// does not fit (regardless of the row-block count).
+// GGUFMM_GEMV_KSPLIT=1: split K over the two CTAs of a cluster whenever the 4-warp
+// shape does not fit; =2: only when the row blocks are too few to give every SM two
+// of them. Off by default: on the 4096 x 14336 down projection the one-CTA 8-warp
+// shape measured 13.4 us per launch against 14.4 us for the split.
 int ksplit_mode() {
   static const int v = [] {
     const char* e = std::getenv("GGUFMM_GEMV_KSPLIT");
-    return e && (e[0] == '0' || e[0] == '1') ? e[0] - '0' : -1;
+    return e && (e[0] == '1' || e[0] == '2') ? e[0] - '0' : 0;
   }();
   return v;
 }
-bool ksplit_disabled() { return ksplit_mode() == 0; }
-int smem_of(int W, int optin) { return std::min(optin, W == 4 ? 113 * 1024 : 227 * 1024); }
+// Shapes: 4 = 4 compute warps, two CTAs per SM; 82 = 8 compute warps, two CTAs per SM
+// (registers capped at 96); 8 = 8 compute warps, one CTA per SM.
+int smem_of(int W, int optin) { return std::min(optin, W == 4 || W == 82 ? 113 * 1024 : 227 * 1024); }
+// GGUFMM_GEMV_SHAPE=8x2 selects the 8-warp two-CTA shape where it fits (tuning).
+bool shape_8x2() {
+  static const bool on = [] {
+    const char* e = std::getenv("GGUFMM_GEMV_SHAPE");
+    return e && e[0] == '8' && e[1] == 'x';
+  }();
+  return on;
+}
 // rowblocks: 16-row blocks of the launch (0 when only asking whether a plan exists).
 int pick_warps(int qt, int64_t k, int m, int optin, I8Args& a, int64_t rowblocks = 0, int sms = 0) {
   const int f = forced_warps();
   if (f) return plan_i8(qt, k, m, smem_of(f, optin), f, 1, a) ? f : 0;
+  if (shape_8x2() && plan_i8(qt, k, m, smem_of(82, optin), 8, 1, a)) return 82;
   if (plan_i8(qt, k, m, smem_of(4, optin), 4, 1, a)) return 4;
-  // Too large for one half-SM CTA: split K over the two CTAs of a cluster when
-  // the row blocks are too few to give every SM two of them (the down
-  // projection); with more row blocks one 8-warp CTA per SM is faster (the DSMEM
-  // exchange and the halved copies cost more than the second CTA gains).
-  const bool few_rows = ksplit_mode() == 1 || (rowblocks > 0 && rowblocks < 2 * static_cast<int64_t>(sms));
+  // Too large for one half-SM CTA: one 8-warp CTA per SM, or -- where even that
+  // does not fit (the activations of M = 8 at K = 14336), or where asked for --
+  // K split over the two CTAs of a cluster.
+  const bool few_rows = rowblocks > 0 && rowblocks < 2 * static_cast<int64_t>(sms);
+  const bool prefer_split = ksplit_mode() == 1 || (ksplit_mode() == 2 && few_rows);
   const bool w8 = plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a);
-  if (!ksplit_disabled() && (few_rows || !w8) && plan_i8(qt, k, m, smem_of(4, optin), 4, 2, a)) return 4;
+  if ((prefer_split || !w8) && plan_i8(qt, k, m, smem_of(4, optin), 4, 2, a)) return 4;
   return w8 && plan_i8(qt, k, m, smem_of(8, optin), 8, 1, a) ? 8 : 0;
 }
 
@@ -1004,9 +1018,9 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   I8Args a{};
   int64_t nrb = 0;
   for (int i = 0; i < nseg; ++i) nrb += (n[i] + kRows - 1) / kRows;
-  const int W = pick_warps(qtype, k, static_cast<int>(m), di.smem_optin, a, nrb, di.sms);
-  if (!W) return cudaErrorInvalidValue;
-  const int optin = smem_of(W, di.smem_optin);
+  const int shape = pick_warps(qtype, k, static_cast<int>(m), di.smem_optin, a, nrb, di.sms);
+  if (!shape) return cudaErrorInvalidValue;
+  const int optin = smem_of(shape, di.smem_optin);
   a.nseg = nseg;
   int64_t rb = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -1039,11 +1053,12 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
   a.ldx = ldx;
   a.m = static_cast<int>(m);
   a.ytype = ytype;
-  if (W == 4) return qtype == kQ4_K ? launch_q<kQ4_K, 4>(a, dev, 2 * di.sms, optin, st)
-                                    : launch_q<kQ4_0, 4>(a, dev, 2 * di.sms, optin, st);
-  if (W == 8) return qtype == kQ4_K ? launch_q<kQ4_K, 8>(a, dev, di.sms, optin, st)
-                                    : launch_q<kQ4_0, 8>(a, dev, di.sms, optin, st);
-  return qtype == kQ4_K ? launch_q<kQ4_K, 16>(a, dev, di.sms, optin, st) : launch_q<kQ4_0, 16>(a, dev, di.sms, optin, st);
+  if (shape == 4) return qtype == kQ4_K ? launch_q<kQ4_K, 4, 2>(a, dev, 2 * di.sms, optin, st)
+                                        : launch_q<kQ4_0, 4, 2>(a, dev, 2 * di.sms, optin, st);
+  if (shape == 82) return qtype == kQ4_K ? launch_q<kQ4_K, 8, 2>(a, dev, 2 * di.sms, optin, st)
+                                         : launch_q<kQ4_0, 8, 2>(a, dev, 2 * di.sms, optin, st);
+  return qtype == kQ4_K ? launch_q<kQ4_K, 8, 1>(a, dev, di.sms, optin, st)
+                        : launch_q<kQ4_0, 8, 1>(a, dev, di.sms, optin, st);
 }
 
 cudaError_t gemv_i8_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }

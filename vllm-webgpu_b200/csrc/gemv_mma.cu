@@ -417,6 +417,7 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
   }
 
   // piece p -> (row block, chunk); 16 rows, one bulk copy per row into the padded stage
+  const uint64_t wpol = l2_evict_first_policy();  // weights are read once per call
   auto issue = [&](int64_t p, int s) {
     const int64_t rb = blockIdx.x + (p / a.nchunks) * gridDim.x;
     const int ch = static_cast<int>(p % a.nchunks);
@@ -429,7 +430,7 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
     const uint8_t* src = sg.q + r0 * a.row_bytes + static_cast<int64_t>(ch) * a.chunk_bytes;
     if (!a.lead) {
       mbar_arrive_expect_tx(&full[s], bytes * nr);
-      for (int r = 0; r < nr; ++r) bulk_g2s(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s]);
+      for (int r = 0; r < nr; ++r) bulk_g2s_hint(dst + r * a.row_pitch, src + r * a.row_bytes, bytes, &full[s], wpol);
       return;
     }
     // Row starts are only 2-byte aligned: copy [start & ~15, end rounded up to 16) of
@@ -455,7 +456,8 @@ __global__ void __launch_bounds__((W + 2) * 32, 1) gemv_mma_kernel(const MmaArgs
       const uintptr_t st = reinterpret_cast<uintptr_t>(src + r * a.row_bytes), en = st + bytes;
       const uintptr_t a0 = st & ~uintptr_t(15);
       const uintptr_t a1 = (last_piece && r == nr - 1) ? (en & ~uintptr_t(15)) : ((en + 15) & ~uintptr_t(15));
-      bulk_g2s(dst + r * a.row_pitch, reinterpret_cast<const void*>(a0), static_cast<uint32_t>(a1 - a0), &full[s]);
+      bulk_g2s_hint(dst + r * a.row_pitch, reinterpret_cast<const void*>(a0), static_cast<uint32_t>(a1 - a0), &full[s],
+                    wpol);
     }
   };
   __syncthreads();  // barriers initialised

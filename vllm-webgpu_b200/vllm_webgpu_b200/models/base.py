@@ -70,18 +70,32 @@ class BaseB200Model:
 
     def _dispatch(self, shader_name: str, bindings: list, constants: dict, workgroups: tuple = (1, 1, 1),
                   shader_subdir: str = "generic") -> None:
-        """Run one kernel. Only the quantized matmul is on this path:
+        """Run one kernel. The quantized matmul and the embedding lookup are on this path:
 
         ``matmul_quant``: bindings = [x, W, scales|unused, out], constants =
         {K, N, USE_QUANT}. x is [tokens, K]; out is a caller-owned [tokens, N]
         tensor written in place. W is a GGUFQuantTensor (any of Q4_0, Q8_0,
         Q4_K, Q6_K) or, with USE_QUANT=0, a dense [N, K] fp16/bf16 tensor.
+        ``embedding_lookup``: bindings = [table, ids, out], constants =
+        {HIDDEN_DIM}; the table is a GGUFQuantTensor (rows dequantized by
+        ggufmm_embedding) or a dense [vocab, hidden] tensor.
         ``workgroups`` is accepted for signature compatibility; the launch
         geometry is the kernels' own.
         """
+        if shader_name == "embedding_lookup":
+            # bindings = [table, token ids, out] (vllm_webgpu/models/llama.py:170-178)
+            table, ids, out = bindings
+            hidden = int(constants["HIDDEN_DIM"])
+            if isinstance(table, GGUFQuantTensor):
+                if table.k != hidden:
+                    raise ValueError(f"embedding_lookup: table rows are {table.k} wide, HIDDEN_DIM={hidden}")
+                ops.embedding(ids, table, out=out.reshape(-1, hidden))
+            else:
+                out.reshape(-1, hidden).copy_(table[ids.reshape(-1).long()])
+            return
         if shader_name != "matmul_quant":
             raise NotImplementedError(
-                f"{shader_subdir}/{shader_name}: only the quantized matmul runs on the B200 path")
+                f"{shader_subdir}/{shader_name}: only the quantized matmul and embedding run on the B200 path")
         x, w, _scales, out = bindings
         k, n = int(constants["K"]), int(constants["N"])
         if isinstance(w, GGUFQuantTensor):

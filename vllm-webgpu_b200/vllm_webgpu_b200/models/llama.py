@@ -128,6 +128,16 @@ class LlamaB200Model(BaseB200Model):
         act_buf.copy_(torch.nn.functional.silu(g) * u)
         return act_buf
 
+    def embed_tokens(self, input_ids: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Token embeddings into ``out`` [tokens, hidden] from ``model.embed_tokens.weight``
+        (GGUF ``token_embd.weight``, quantized in a GGUF file), as the reference's
+        ``_dispatch("embedding_lookup", [table, ids, x], {HIDDEN_DIM})`` (llama.py:170-178)."""
+        table = self.weights["model.embed_tokens.weight"]
+        hidden = table.k if isinstance(table, GGUFQuantTensor) else table.shape[1]
+        self._dispatch("embedding_lookup", [table, input_ids, out], {"HIDDEN_DIM": hidden},
+                       (input_ids.numel(), 1, 1))
+        return out
+
     def project_lm_head(self, hidden: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
         """Logits from the final hidden state on the GGUF output weight (``lm_head.weight``,
         GGUF ``output.weight``), quantized like the other projections (the reference

@@ -75,6 +75,29 @@ def dequantize(w: GGUFQuantTensor, out_dtype: torch.dtype = torch.float32,
     return out
 
 
+def embedding(ids: torch.Tensor, table: GGUFQuantTensor, out: torch.Tensor | None = None,
+              out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Rows ``ids`` of a GGUF-quantized embedding table, dequantized: out[t, :] =
+    table[ids[t], :]. Replaces the reference's ``embedding_lookup`` dispatch
+    (vllm_webgpu/models/llama.py:170-178), which copied rows of an f16 table.
+    float32 output is bit-identical to gguf.quants.dequantize of the row. An id
+    outside the table gives a zero row and sets bit 2 of the device status word."""
+    dev = _require_cuda(ids, table.data)
+    ids32 = ids.reshape(-1)
+    if ids32.dtype != torch.int32 or not ids32.is_contiguous():
+        ids32 = ids32.to(torch.int32).contiguous()
+    n_ids = ids32.numel()
+    if out is None:
+        out = torch.empty((n_ids, table.k), dtype=out_dtype, device=dev)
+    elif out.dim() != 2 or out.shape != (n_ids, table.k) or out.stride(1) != 1:
+        raise ValueError(f"out must be a row-major [{n_ids}, {table.k}] tensor")
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_embedding(table.data.data_ptr(), table.qtype, table.n, table.k, ids32.data_ptr(),
+                                         n_ids, out.data_ptr(), _code(out.dtype), out.stride(0), _stream(dev))
+    _lib.check(st, "ggufmm_embedding")
+    return out
+
+
 def gemv(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
          out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Decode GEMV, M <= 8 tokens: out[m, n] = sum_k x[m, k] W[n, k]."""
