@@ -133,3 +133,21 @@ def test_dispatch_boundary_errors():
         m._dispatch("matmul_quant", [x, w, None, torch.zeros((1, 8))], {"K": 256, "N": 8, "USE_QUANT": 1})
     with pytest.raises(ValueError, match="CUDA"):  # right shapes, but the kernels run on CUDA tensors only
         m._dispatch("matmul_quant", [x, w, None, torch.zeros((1, 4))], {"K": 256, "N": 4, "USE_QUANT": 1})
+
+
+def test_build_model_follows_the_reference_arch_map():
+    """Architecture -> model family as the reference's ARCH_MAP
+    (vllm_webgpu/v1/model_runner.py:32-53)."""
+    from types import SimpleNamespace
+
+    from vllm_webgpu_b200.models.gemma4 import ARCH_MAP, Gemma4B200Model, build_model
+    from vllm_webgpu_b200.models.llama import LlamaB200Model
+    cfg = SimpleNamespace(hidden_size=2560, num_attention_heads=8, num_key_value_heads=2, head_dim=256)
+    assert type(build_model("LlamaForCausalLM", None, device="cpu")) is LlamaB200Model
+    assert type(build_model("Qwen2ForCausalLM", None, device="cpu")) is LlamaB200Model
+    g = build_model("Gemma3ForCausalLM", cfg, device="cpu")
+    assert isinstance(g, Gemma4B200Model) and g.q_dim == 2048 and g.kv_dim == 512
+    assert set(ARCH_MAP) == {"LlamaForCausalLM", "MistralForCausalLM", "Qwen2ForCausalLM", "Qwen3ForCausalLM",
+                             "Gemma3ForCausalLM"}
+    with pytest.raises(NotImplementedError):
+        build_model("GPT2LMHeadModel", None, device="cpu")
