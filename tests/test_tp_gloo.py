@@ -92,3 +92,73 @@ def test_shard_ranges_and_errors():
     assert gl.shape == (I // 2, H) and dl.shape == (H, I // 2)
     full = O.dequantize(d.data.numpy(), O.Q4_K, H, I)
     assert np.array_equal(O.dequantize(dl.data.numpy(), O.Q4_K, H, I // 2), full[:, I // 2:])
+
+
+# ---- the layer's seven projections split over ranks (TensorParallelLayerLinears) ----
+LH, LI, LKV = 1024, 2048, 256  # hidden, intermediate, k/v width of a small Llama-like layer (splits stay
+# superblock-aligned up to 4 ranks)
+
+
+def _layer_weights():
+    from vllm_webgpu_b200.formats import GGUFQuantTensor
+    shapes = {"q": (LH, LH), "k": (LKV, LH), "v": (LKV, LH), "o": (LH, LH), "gate": (LI, LH), "up": (LI, LH),
+              "down": (LH, LI)}
+    return {p: GGUFQuantTensor(torch.from_numpy(O.make_weights(n, k, O.Q4_K, seed=20 + i)), O.Q4_K, (n, k))
+            for i, (p, (n, k)) in enumerate(shapes.items())}
+
+
+def _layer_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from vllm_webgpu_b200.tp import TensorParallelLayerLinears
+        ws = _layer_weights()
+        tpl = TensorParallelLayerLinears(ws, rank=rank, world=world, matmul=_oracle_matmul)
+        xs = {nm: torch.from_numpy(O.make_activations(2, k, seed=30 + j))
+              for j, (nm, k) in enumerate((("normed", LH), ("attn", LH), ("ffn", LH), ("act", LI)))}
+        h0, h1 = rank * LH // world, (rank + 1) * LH // world
+        i0, i1 = rank * LI // world, (rank + 1) * LI // world
+        bufs = {p: torch.empty((2, tpl.w[p].n), dtype=torch.float32) for p in ("q", "k", "v", "gate", "up")}
+        bufs["o"] = torch.empty((2, LH), dtype=torch.float32)
+        bufs["down"] = torch.empty((2, LH), dtype=torch.float32)
+        tpl(xs["normed"], xs["attn"][:, h0:h1], xs["ffn"], xs["act"][:, i0:i1], bufs)
+        q.put((rank, {p: b.numpy() for p, b in bufs.items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_layer_linears_gloo(world):
+    import queue
+    import time as _t
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_layer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    got = {}
+    deadline = _t.monotonic() + 240
+    while len(got) < world:
+        try:
+            r, v = q.get(timeout=5)
+            got[r] = v
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in ps) or _t.monotonic() > deadline:
+                for p in ps:
+                    p.kill()
+                pytest.fail(f"a rank failed: exit codes {[p.exitcode for p in ps]}")
+    for p in ps:
+        p.join(60)
+    ws = _layer_weights()
+    xs = {nm: O.make_activations(2, k, seed=30 + j)
+          for j, (nm, k) in enumerate((("normed", LH), ("attn", LH), ("ffn", LH), ("act", LI)))}
+    src = {"q": "normed", "k": "normed", "v": "normed", "o": "attn", "gate": "ffn", "up": "ffn", "down": "act"}
+    for p, w in ws.items():
+        ref = O.matmul_ref(xs[src[p]], w.data.numpy(), w.qtype, w.n, w.k)
+        if p in ("o", "down"):  # all-reduced: every rank holds the full sum
+            for r in range(world):
+                assert O.rel_err(got[r][p], ref) <= 1e-5, (p, r)
+        else:  # output-row slices, concatenated in rank order
+            full = np.concatenate([got[r][p] for r in range(world)], axis=1)
+            assert O.rel_err(full, ref) <= 1e-5, p

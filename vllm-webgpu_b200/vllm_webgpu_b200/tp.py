@@ -134,3 +134,110 @@ class TensorParallelSwiGLU:
             return None
 
     __call__ = forward
+
+
+class TensorParallelLayerLinears:
+    """The seven projections of one Llama layer split over ``world`` ranks (the
+    Megatron split that keeps attention and the SwiGLU local to a rank):
+
+    * q, k, v and gate, up by OUTPUT rows (a row slice of each GGUF byte matrix:
+      rank r owns heads / intermediate features [r N/P, (r+1) N/P));
+    * o and down by INPUT columns over the same ranges (superblock-aligned
+      column slices), so each rank's o / down partial is summed by ONE
+      all-reduce each (NCCL over NVLink, fp32: a bf16 partial would round each
+      rank's sum by up to 2^-9 relative, the size of the 2e-3 gate itself).
+
+    The reference calls these projections one dispatch each on a single device
+    (vllm_webgpu/models/llama.py:276-283, 328-332, 343-348, 355-359); with
+    world = 1 this class runs exactly those calls. ``forward`` takes the
+    rank-local activations: ``attn_local`` is this rank's slice of the attention
+    output (its heads), ``act_local`` its slice of the SwiGLU activation.
+    """
+
+    NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+
+    def __init__(self, weights: dict, rank: int = 0, world: int = 1, group=None, matmul: Callable | None = None):
+        self.rank, self.world, self.group = rank, world, group
+        self.matmul = matmul  # injectable (CPU tests); the GPU path uses the grouped kernels
+        self.collective = True  # False leaves out the all-reduces (measuring what they cost)
+        self._graphs: dict = {}
+        w = {}
+        for p in ("q", "k", "v", "gate", "up"):
+            n = weights[p].n
+            r0, r1 = shard_range(n, rank, world, 16)
+            w[p] = weights[p] if world == 1 else weights[p].rows(r0, r1)
+        for p in ("o", "down"):
+            k = weights[p].k
+            block = QUANT_SIZES[weights[p].qtype][1]
+            c0, c1 = shard_range(k, rank, world, block)
+            w[p] = weights[p] if world == 1 else weights[p].cols(c0, c1)
+        self.w = w
+
+    def _mm(self, x, w, out) -> None:
+        if self.matmul is not None:
+            out.copy_(self.matmul(x, w, out_dtype=out.dtype).reshape(out.shape))
+            return
+        from . import ops
+        ops.mul_mat(x, w, out=out)
+
+    def _grouped(self, x: torch.Tensor, ps, outs) -> None:
+        if self.matmul is not None:
+            for p, o in zip(ps, outs):
+                self._mm(x, self.w[p], o)
+            return
+        from . import ops
+        ws = [self.w[p] for p in ps]
+        m = x.reshape(-1, x.shape[-1]).shape[0]
+        if len({w.qtype for w in ws}) == 1 and ops.gemv_preferred(m, ws[0], x.dtype):
+            ops.gemv_grouped(x, ws, outs=outs)
+        elif len({w.qtype for w in ws}) == 1:
+            ops.gemm_grouped(x, ws, outs=outs)
+        else:
+            for w, o in zip(ws, outs):
+                ops.mul_mat(x, w, out=o)
+
+    def forward(self, normed, attn_local, ffn_normed, act_local, bufs: dict) -> dict:
+        """bufs: q, k, v, gate, up (this rank's output slices) and o, down (full
+        width, fp32: the all-reduced sums)."""
+        self._grouped(normed, ("q", "k", "v"), [bufs["q"], bufs["k"], bufs["v"]])
+        self._mm(attn_local, self.w["o"], bufs["o"])
+        if self.world > 1 and self.collective:
+            dist.all_reduce(bufs["o"], op=dist.ReduceOp.SUM, group=self.group)
+        self._grouped(ffn_normed, ("gate", "up"), [bufs["gate"], bufs["up"]])
+        self._mm(act_local, self.w["down"], bufs["down"])
+        if self.world > 1 and self.collective:
+            dist.all_reduce(bufs["down"], op=dist.ReduceOp.SUM, group=self.group)
+        return bufs
+
+    __call__ = forward
+
+    def graph_step(self, normed, attn_local, ffn_normed, act_local, bufs: dict, stage_in=(), stage_out=()) -> dict:
+        """``forward`` replayed from a CUDA graph (captured on the first call for these
+        buffers), with optional (destination, source) host <-> device copies of pinned
+        buffers captured before and after it: the decode serving loop, one replay per
+        step (the NCCL all-reduces are captured with the launches)."""
+        stage_in, stage_out = list(stage_in), list(stage_out)
+        key = (normed.data_ptr(), attn_local.data_ptr(), ffn_normed.data_ptr(), act_local.data_ptr(),
+               tuple((k, b.data_ptr()) for k, b in sorted(bufs.items())),
+               tuple((d.data_ptr(), s.data_ptr()) for d, s in stage_in + stage_out))
+        g = self._graphs.get(key)
+
+        def body():
+            for dst, src in stage_in:
+                dst.copy_(src, non_blocking=True)
+            self.forward(normed, attn_local, ffn_normed, act_local, bufs)
+            for dst, src in stage_out:
+                dst.copy_(src, non_blocking=True)
+        if g is None:
+            cur = torch.cuda.current_stream()
+            side = torch.cuda.Stream()
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                body()  # warm-up
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                body()
+            cur.wait_stream(side)
+            self._graphs[key] = g
+        g.replay()
+        return bufs
