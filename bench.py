@@ -19,9 +19,13 @@ step), ``roofline`` for the dominant kernel, ``prefill`` (config 4 tensor-core
 GEMM TFLOP/s), ``cpu_baseline`` (the reference's CPU arithmetic: gguf-py
 dequantize + numpy fp32 matmul on a bounded sample) and sampled clocks.
 
-Multi-GPU (torchrun, one process per GPU): every rank decodes its own layer
-(independent weights, no collective in the data path) -> weak scaling;
-value = all ranks' bytes / max-over-ranks time.
+Multi-GPU (torchrun, one process per GPU): the same layer split over the ranks
+(TensorParallelLayerLinears: q/k/v and gate/up by output rows, o and down by
+input columns, one NCCL all-reduce after each) -> strong scaling; value = one
+layer's bytes per step / the max-over-ranks time, with the all-reduces' share of
+the step reported in ``comm``. The config-4 prefill GEMM splits N over the ranks
+with an NCCL all-gather of the outputs; the config-5 FFN splits its intermediate
+dimension with one all-reduce.
 
 ``--impl reference`` times the reference's own CPU path for the same metric:
 gguf.quants.dequantize (gguf-py, the reference's pinned dependency) followed
@@ -244,7 +248,7 @@ def run_reference(args, rank: int, world: int) -> None:
     line = {
         "metric": METRIC, "value": round(res["value"], 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(res["ms_per_step"], 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u4 x fp32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u4 x fp32",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
                    "parallelism": "rank 0 only (CPU)", "rows_per_projection_per_step": res["rows"]},
@@ -270,29 +274,41 @@ def run_ours(args, rank: int, world: int) -> None:
     peaks, peak_src = load_peaks()
     m = 1
     copies = 3
-    # weights: 3 independent copies of the layer (seeded per rank and copy)
-    layers = []
+    # weights: 3 copies of the layer (the same seeds on every rank), each split over the
+    # ranks Megatron-style by TensorParallelLayerLinears: q/k/v and gate/up by output rows,
+    # o and down by input columns with one NCCL all-reduce each. At world 1 it runs the
+    # layer's four launches unsplit.
+    from vllm_webgpu_b200.tp import TensorParallelLayerLinears
+    NAMES = ("q", "k", "v", "o", "gate", "up", "down")
+    tps, layers = [], []
     for c in range(copies):
-        layers.append([random_weights(n, k, Q4_K, seed=1000 * rank + 10 * c + i, device=dev)
-                       for i, (_, n, k) in enumerate(LAYER)])
+        full = {p: random_weights(n, k, Q4_K, seed=10 * c + i, device=dev)
+                for i, (p, (_, n, k)) in enumerate(zip(NAMES, LAYER))}
+        tps.append(TensorParallelLayerLinears(full, rank=rank, world=world))
+        layers.append([full[p] for p in NAMES] if world == 1 else None)
+        del full
     g = torch.Generator(device=dev)
-    g.manual_seed(7 + rank)
-    xs = {k: torch.randn((m, k), generator=g, device=dev).to(torch.bfloat16) for k in (4096, 14336)}
-    ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _, n, _ in LAYER]
+    g.manual_seed(7)
+    hid, inter = 4096, 14336
+    xs = {"normed": torch.randn((m, hid), generator=g, device=dev).to(torch.bfloat16),
+          "attn": torch.randn((m, hid), generator=g, device=dev).to(torch.bfloat16),
+          "ffn": torch.randn((m, hid), generator=g, device=dev).to(torch.bfloat16),
+          "act": torch.randn((m, inter), generator=g, device=dev).to(torch.bfloat16)}
+    h0, h1 = rank * hid // world, (rank + 1) * hid // world
+    i0, i1 = rank * inter // world, (rank + 1) * inter // world
+    attn_local = xs["attn"][:, h0:h1].contiguous()
+    act_local = xs["act"][:, i0:i1].contiguous()
+    tp0 = tps[0]
+    bufs = {p: torch.empty((m, tp0.w[p].n), dtype=torch.float32, device=dev) for p in ("q", "k", "v", "gate", "up")}
+    bufs["o"] = torch.empty((m, hid), dtype=torch.float32, device=dev)
+    bufs["down"] = torch.empty((m, hid), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def launch(c: int, grp) -> None:
-        _, idx, k = grp
-        if len(idx) == 1:
-            ops.gemv(xs[k], layers[c][idx[0]], out=ys[idx[0]])
-        else:
-            ops.gemv_grouped(xs[k], [layers[c][i] for i in idx], outs=[ys[i] for i in idx])
+    def step(c: int, collective: bool = True) -> None:
+        tps[c].collective = collective
+        tps[c](xs["normed"], attn_local, xs["ffn"], act_local, bufs)
 
-    def step(c: int) -> None:
-        for grp in GROUPS:
-            launch(c, grp)
-
-    # warm-up (also primes attributes / driver entry points before capture)
+    # warm-up (also primes attributes / driver entry points / NCCL before capture)
     for i in range(max(3, args.warmup)):
         step(i % copies)
     torch.cuda.synchronize()
@@ -300,11 +316,13 @@ def run_ours(args, rank: int, world: int) -> None:
     # CUDA graphs of consecutive steps over the rotating weight copies (launch overhead
     # out of the device time): a 30-step graph replayed, plus one graph for the
     # remainder, so exactly --steps steps are timed
-    def capture(nsteps: int, first: int = 0):
+    def capture(nsteps: int, collective: bool = True):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
             for i in range(nsteps):
-                step((first + i) % copies)
+                step(i % copies, collective)
+        for c in range(copies):
+            tps[c].collective = True
         return gr
     chunk = 30
     big = capture(chunk)
@@ -313,46 +331,74 @@ def run_ours(args, rank: int, world: int) -> None:
     for _ in range(3):
         big.replay()
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def timed_run() -> float:
+    def timed_run(gbig=None, gsmall=None) -> float:
+        if gbig is None:
+            gbig, gsmall = big, small
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(reps):
-            big.replay()
-        if small is not None:
-            small.replay()
+            gbig.replay()
+        if gsmall is not None:
+            gsmall.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         return e0.elapsed_time(e1)
 
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     steps = args.steps
     # a timed region shorter than ~250 ms is repeated (same K steps each time) so the
     # clock sampler sees it under load; the median repeat is reported
     est = timed_run()
-    repeats = max(1, min(200, int(250.0 / max(est, 1e-3)) + 1))
-    if world > 1:
-        t = torch.tensor([repeats], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        repeats = int(t.item())
-        dist.barrier()
-    torch.cuda.synchronize()
+    repeats = int(max_over_ranks(max(1, min(200, int(250.0 / max(est, 1e-3)) + 1))))
     runs = []
     with ClockSampler(local) as clk:
         for _ in range(repeats):
             runs.append(timed_run())
-    ms = statistics.median(runs)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
+    ms = max_over_ranks(statistics.median(runs))
     step_bytes = layer_bytes(m, act_bytes=2, out_bytes=4)
-    value = step_bytes * steps * world / (ms / 1e3) / 1e9
+    # strong scaling: one layer's bytes per step whatever the rank count
+    value = step_bytes * steps / (ms / 1e3) / 1e9
+    comm = None
+    if world > 1:
+        # the same steps without the two all-reduces: what the collectives cost
+        nb = capture(chunk, collective=False)
+        ns = capture(rem, collective=False) if rem else None
+        nb.replay()
+        torch.cuda.synchronize()
+        ms_nc = max_over_ranks(statistics.median([timed_run(nb, ns) for _ in range(max(1, repeats // 2))]))
+        comm = {"step_us_without_allreduce": round(ms_nc / steps * 1e3, 2),
+                "allreduce_share_of_step": round(max(0.0, 1.0 - ms_nc / ms), 4),
+                "allreduces_per_step": 2, "allreduce_bytes": m * hid * 4, "collective": "NCCL all_reduce (fp32)"}
+        del nb, ns
 
-    # per-launch device time of the dominant kernel (every launch is gemv_i8_kernel<Q4_K>):
-    # each group alone in a CUDA graph of 30 launches over the rotating copies
-    per = {}
-    for grp in GROUPS:
+    # per-launch device time of each launch of the (local) step, each alone in a CUDA
+    # graph of 30 launches over the rotating copies; bytes are this rank's share
+    LOCAL_GROUPS = [("qkv", ("q", "k", "v"), "normed"), ("o", ("o",), "attn"), ("gate_up", ("gate", "up"), "ffn"),
+                    ("down", ("down",), "act")]
+    xin = {"normed": xs["normed"], "attn": attn_local, "ffn": xs["ffn"], "act": act_local}
+
+    def launch(c: int, grp) -> None:
+        _, ps, xn = grp
+        if len(ps) == 1:
+            ops.mul_mat(xin[xn], tps[c].w[ps[0]], out=bufs[ps[0]])
+        else:
+            ops.gemv_grouped(xin[xn], [tps[c].w[p] for p in ps], outs=[bufs[p] for p in ps])
+
+    def group_bytes(ps, xn) -> int:
+        ws = [tp0.w[p] for p in ps]
+        return sum(w.nbytes + m * w.n * 4 for w in ws) + m * xin[xn].shape[1] * 2
+    per, per_bytes = {}, {}
+    for grp in LOCAL_GROUPS:
         gg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gg):
             for r in range(30):
@@ -365,25 +411,29 @@ def run_ours(args, rank: int, world: int) -> None:
         e1.record(stream)
         torch.cuda.synchronize()
         per[grp[0]] = e0.elapsed_time(e1) / 150
+        per_bytes[grp[0]] = group_bytes(grp[1], grp[2])
+        del gg
     kern_ms = sum(per.values())
-    achieved = step_bytes / (kern_ms / 1e3) / 1e9
+    local_bytes = sum(per_bytes.values())
+    achieved = local_bytes / (kern_ms / 1e3) / 1e9
+    per_frac = {nm: round(per_bytes[nm] / (per[nm] / 1e3) / 1e9 / float(peaks["hbm_gbs"]), 4) for nm in per}
 
-    def group_bytes(idx, k) -> int:
-        return sum(LAYER[i][1] * k // 256 * 144 + m * k * 2 + m * LAYER[i][1] * 4 for i in idx) - (len(idx) - 1) * m * k * 2
-    per_frac = {nm: round(group_bytes(idx, k) / (per[nm] / 1e3) / 1e9 / float(peaks["hbm_gbs"]), 4)
-                for nm, idx, k in GROUPS}
-
-    # end to end through the public model API (LlamaB200Model.layer_linears_graph: the
-    # reference's per-layer projection calls, replayed from a CUDA graph as a decode
-    # serving loop does): every step copies the activations in from pinned host memory
-    # (one packed copy), runs the layer's projections and reads all outputs back (one
-    # packed copy), then waits for them on the host
-    from vllm_webgpu_b200.models.llama import PROJ, LlamaB200Model
-    model = LlamaB200Model(None, device=dev)
-    for c in range(copies):
-        for i, (nm, _, _) in enumerate(LAYER):
-            model.weights[f"model.layers.{c}.{PROJ[nm.split('_')[0]]}"] = layers[c][i]
-    in_dims = (("normed", 4096), ("attn_out", 4096), ("ffn_normed", 4096), ("ffn_act", 14336))
+    # end to end through the public API, one CUDA-graph replay per step that copies the
+    # step's activations in from pinned host memory (one packed copy), runs the layer's
+    # projections (and, at N > 1, the all-reduces) and copies every output back (one
+    # packed copy), then a host wait. N = 1: LlamaB200Model.layer_linears_graph (the
+    # reference's per-layer projection calls); N > 1: TensorParallelLayerLinears.graph_step.
+    if world == 1:
+        from vllm_webgpu_b200.models.llama import PROJ, LlamaB200Model
+        model = LlamaB200Model(None, device=dev)
+        for c in range(copies):
+            for i, (nm, _, _) in enumerate(LAYER):
+                model.weights[f"model.layers.{c}.{PROJ[nm.split('_')[0]]}"] = layers[c][i]
+        in_dims = (("normed", hid), ("attn_out", hid), ("ffn_normed", hid), ("ffn_act", inter))
+        out_dims = [(nm.split("_")[0], n) for nm, n, _ in LAYER]
+    else:
+        in_dims = (("normed", hid), ("attn_out", h1 - h0), ("ffn_normed", hid), ("ffn_act", i1 - i0))
+        out_dims = [(p, tp0.w[p].n) for p in ("q", "k", "v", "gate", "up")] + [("o", hid), ("down", hid)]
     kin = sum(kk for _, kk in in_dims)
     hin = torch.randn((m, kin)).to(torch.bfloat16).pin_memory()
     din = torch.empty((m, kin), dtype=torch.bfloat16, device=dev)
@@ -391,21 +441,28 @@ def run_ours(args, rank: int, world: int) -> None:
     for nm, kk in in_dims:
         d[nm] = din[:, off:off + kk]
         off += kk
-    nout = sum(n for _, n, _ in LAYER)
+    nout = sum(n for _, n in out_dims)
     dout = torch.empty((nout * m,), dtype=torch.float32, device=dev)
     hout = torch.empty_like(dout, device="cpu").pin_memory()
-    bufs, off = {}, 0
-    for nm, n, _ in LAYER:
-        bufs[nm.split("_")[0]] = dout[off:off + m * n].view(m, n)
+    ebufs, off = {}, 0
+    for nm, n in out_dims:
+        ebufs[nm] = dout[off:off + m * n].view(m, n)
         off += m * n
     e2e_steps = max(30, min(2000, steps // 10))
     h2d = hin.numel() * 2
     d2h = dout.numel() * 4
 
+    def run_graph(c: int, stage: bool) -> None:
+        si, so = ([(din, hin)], [(hout, dout)]) if stage else ((), ())
+        if world == 1:
+            model.layer_linears_graph(c, d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], ebufs,
+                                      stage_in=si, stage_out=so)
+        else:
+            tps[c].graph_step(d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], ebufs, stage_in=si,
+                              stage_out=so)
+
     def e2e_step(c: int) -> None:
-        # one graph replay: H2D of the step's activations, the projections, D2H of the outputs
-        model.layer_linears_graph(c, d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], bufs,
-                                  stage_in=[(din, hin)], stage_out=[(hout, dout)])
+        run_graph(c, True)
         stream.synchronize()
 
     for i in range(5):
@@ -418,16 +475,15 @@ def run_ours(args, rank: int, world: int) -> None:
         e2e_step(i % copies)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = step_bytes * e2e_steps * world / (e2e_ms / 1e3) / 1e9
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9
+
     # where an end-to-end step goes: each part alone with a host wait, host wall clock
     def host_us(fn, n=200) -> float:
         for _ in range(5):
             fn()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
         for _ in range(n):
             fn()
@@ -438,7 +494,7 @@ def run_ours(args, rank: int, world: int) -> None:
         stream.synchronize()
 
     def only_graph():
-        model.layer_linears_graph(0, d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], bufs)
+        run_graph(0, False)
         stream.synchronize()
 
     def only_d2h():
@@ -447,42 +503,69 @@ def run_ours(args, rank: int, world: int) -> None:
     e2e_parts = {"h2d_and_wait_us": round(host_us(only_h2d), 2), "graph_replay_and_wait_us": round(host_us(only_graph), 2),
                  "d2h_and_wait_us": round(host_us(only_d2h), 2), "step_us": round(e2e_ms / e2e_steps * 1e3, 2),
                  "device_step_us": round(ms / steps * 1e3, 2)}
+    del ebufs
 
     # prefill (config 4): Q4_K / Q6_K GEMM, K=4096, N=14336, M in {512, 2048, 8192} on the
-    # tensor cores, bf16 out; the headline key is Q4_K at M = 2048
+    # tensor cores, bf16 out; the headline key is Q4_K at M = 2048. At N > 1 the weight's
+    # N dimension is split over the ranks (each computes [M, N/P]) and an NCCL
+    # all-gather collects the [P, M, N/P] outputs on every rank; TFLOP/s is the whole
+    # GEMM's 2 M N K over the max-over-ranks time, with the all-gather's share reported.
     pre = None
     prefill_sweep = None
     if not args.no_prefill:
         pn, pk = 14336, 4096
-        wts = {Q4_K: layers[0][4], 14: random_weights(pn, pk, 14, seed=77 + rank, device=dev)}
+        r0, r1 = rank * pn // world, (rank + 1) * pn // world
+        wts = {}
+        for qt, sd in ((Q4_K, 4), (14, 77)):
+            wfull = random_weights(pn, pk, qt, seed=sd, device=dev)
+            wts[qt] = wfull if world == 1 else wfull.rows(r0, r1)
+            del wfull
         prefill_sweep = {}
         for qt, qname in ((Q4_K, "q4_k"), (14, "q6_k")):
             for pm in (512, 2048, 8192):
                 xp = torch.randn((pm, pk), device=dev).to(torch.bfloat16)
-                yp = torch.empty((pm, pn), dtype=torch.bfloat16, device=dev)
-                for _ in range(3):
+                yp = torch.empty((pm, r1 - r0), dtype=torch.bfloat16, device=dev)
+                yg = torch.empty((world * pm, r1 - r0), dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+                def pstep(gather: bool = True) -> None:
                     ops.gemm(xp, wts[qt], out=yp)
+                    if world > 1 and gather:
+                        dist.all_gather_into_tensor(yg, yp)
+                for _ in range(3):
+                    pstep()
                 torch.cuda.synchronize()
                 it = max(3, int(2e12 / (2.0 * pm * pn * pk)))  # ~10 ms of work at least
-                e0.record(stream)
-                for _ in range(it):
-                    ops.gemm(xp, wts[qt], out=yp)
-                e1.record(stream)
-                torch.cuda.synchronize()
-                pms = e0.elapsed_time(e1) / it
+
+                def ptime(gather: bool) -> float:
+                    if world > 1:
+                        dist.barrier()
+                    torch.cuda.synchronize()
+                    e0.record(stream)
+                    for _ in range(it):
+                        pstep(gather)
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    return max_over_ranks(e0.elapsed_time(e1) / it)
+                pms = ptime(True)
                 tf = 2.0 * pm * pn * pk / (pms / 1e3) / 1e12
-                prefill_sweep[f"{qname}_m{pm}"] = {"ms": round(pms, 4), "tflops": round(tf, 2),
-                                                   "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 4)}
-                del xp, yp
+                rec = {"ms": round(pms, 4), "tflops": round(tf, 2),
+                       "frac_of_bf16_peak": round(tf / world / peaks["bf16_tflops"], 4)}
+                if world > 1:
+                    pms_ng = ptime(False)
+                    rec["allgather_share"] = round(max(0.0, 1.0 - pms_ng / pms), 4)
+                    rec["ms_without_allgather"] = round(pms_ng, 4)
+                prefill_sweep[f"{qname}_m{pm}"] = rec
+                del xp, yp, yg
         p2 = prefill_sweep["q4_k_m2048"]
         pre = {"workload": "q4k_prefill_m2048_k4096_n14336", **p2,
-               "path": "dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"}
+               "path": ("dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"
+                        + ("" if world == 1 else f"; N split over {world} ranks + NCCL all_gather of the outputs"))}
         del wts
 
     # BASELINE configs 1 and 2 on the GPU: Q8_0 4096 x 4096 matvec with fp32 x, and the
     # Q4_0 14336 x 4096 GEMV at M in {1, 4, 8} with fp16 x; weight copies rotated past L2
     other = None
-    if not args.no_configs:
+    if not args.no_configs and world == 1:
         other = {}
         for key, qt, n, k, ms_, xdt, ncopy in (("config1_q8_0_matvec_f32", 8, 4096, 4096, (1,), torch.float32, 8),
                                               ("config2_q4_0_gemv_f16", 2, 14336, 4096, (1, 4, 8), torch.float16, 5)):
@@ -513,25 +596,25 @@ def run_ours(args, rank: int, world: int) -> None:
                                         "kernel": ["stream", "f16_tc", "int8_tc"][ops.gemv_kernel(mm, ws_[0], xdt)]}
             del ws_
 
-    # batched decode of the same layer (config 3 at M = 16 and 64): the model's path above
-    # M = 8 -- q/k/v and gate/up as grouped fused-dequant tcgen05 GEMMs, o and down through
-    # ops.mul_mat -- replayed from a CUDA graph over the rotating weight copies
+    # batched decode of the same layer (config 3 at M = 16 and 64): above M = 8 q/k/v and
+    # gate/up run as grouped fused-dequant tcgen05 GEMMs, o and down through ops.mul_mat
+    # (split over the ranks with the all-reduces at N > 1), replayed from a CUDA graph
+    # over the rotating weight copies
     batched = None
     if not args.no_batched:
         batched = {"workload": "q4k_llama3_8b_layer_decode", "path": "4 launch groups: ops.gemm_grouped (q/k/v, "
                    "gate/up) and ops.mul_mat (o, down); fused-dequant tcgen05 GEMM, K split where the "
-                   "weights have few 128-row tiles"}
+                   "weights have few 128-row tiles" + ("" if world == 1 else f"; tp{world} with 2 NCCL all-reduces")}
         wbytes = sum(n * k // 256 * 144 for _, n, k in LAYER)
         for mb in (16, 64):
-            xb = {kk: torch.randn((mb, kk), generator=g, device=dev).to(torch.bfloat16) for kk in (4096, 14336)}
-            yb = [torch.empty((mb, n), dtype=torch.bfloat16, device=dev) for _, n, _ in LAYER]
+            xb = {nm: torch.randn((mb, kk), generator=g, device=dev).to(torch.bfloat16)
+                  for nm, kk in (("normed", hid), ("attn", h1 - h0), ("ffn", hid), ("act", i1 - i0))}
+            yb = {p: torch.empty((mb, tp0.w[p].n), dtype=torch.bfloat16, device=dev) for p in ("q", "k", "v", "gate", "up")}
+            yb["o"] = torch.empty((mb, hid), dtype=torch.float32, device=dev)
+            yb["down"] = torch.empty((mb, hid), dtype=torch.float32, device=dev)
 
             def bstep(c: int) -> None:
-                for _, idx, kk in GROUPS:
-                    if len(idx) == 1:
-                        ops.mul_mat(xb[kk], layers[c][idx[0]], out=yb[idx[0]])
-                    else:
-                        ops.gemm_grouped(xb[kk], [layers[c][i] for i in idx], outs=[yb[i] for i in idx])
+                tps[c](xb["normed"], xb["attn"], xb["ffn"], xb["act"], yb)
 
             for i in range(3):
                 bstep(i % copies)
@@ -541,6 +624,8 @@ def run_ours(args, rank: int, world: int) -> None:
                 for c in range(copies):
                     bstep(c)
             bg.replay()
+            if world > 1:
+                dist.barrier()
             torch.cuda.synchronize()
             reps_b = 20
             e0.record(stream)
@@ -548,13 +633,13 @@ def run_ours(args, rank: int, world: int) -> None:
                 bg.replay()
             e1.record(stream)
             torch.cuda.synchronize()
-            bms = e0.elapsed_time(e1) / (reps_b * copies)
+            bms = max_over_ranks(e0.elapsed_time(e1) / (reps_b * copies))
             batched[f"m{mb}"] = {"us_per_step": round(bms * 1e3, 2), "weight_gbs": round(wbytes / (bms / 1e3) / 1e9, 2),
                                  "tflops": round(2.0 * mb * wbytes / 144 * 256 / (bms / 1e3) / 1e12, 2)}
             del bg
 
     # tensor-parallel SwiGLU FFN (config 5): Llama-3-70B shape, Q4_K, intermediate split over
-    # the ranks, one NCCL all-reduce per step (decode M=1 and M=32); eager, host-issued steps
+    # the ranks, one NCCL all-reduce per step, M in {1, 32, 2048}
     tpf = None
     if not args.no_tp:
         from vllm_webgpu_b200.tp import TensorParallelSwiGLU
@@ -565,26 +650,34 @@ def run_ours(args, rank: int, world: int) -> None:
         del full
         wbytes = 3 * hid * inter // 256 * 144
         tpf = {"workload": "q4k_llama3_70b_ffn_tp", "tp": world, "weight_bytes_total": wbytes,
-               "path": "fused gate/up/SwiGLU GEMV (M<=8) or GEMMs, down projection, NCCL all-reduce"}
-        for mt in (1, 32):
+               "path": "fused gate/up/SwiGLU GEMV (M<=8) or GEMMs, down projection, NCCL all-reduce; CUDA graph replay"}
+        for mt in (1, 32, 2048):
             xt = torch.randn((mt, hid), generator=g, device=dev).to(torch.bfloat16)
             for _ in range(3):
                 ffn(xt)
+            torch.cuda.synchronize()
+            # captured as a CUDA graph (the NCCL all-reduce included), replayed
+            reps_f = 10 if mt <= 32 else 2
+            fg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(fg):
+                for _ in range(reps_f):
+                    ffn(xt)
+            fg.replay()
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
-            it = 50
+            it = 10
             e0.record(stream)
             for _ in range(it):
-                ffn(xt)
+                fg.replay()
             e1.record(stream)
             torch.cuda.synchronize()
-            tms = e0.elapsed_time(e1) / it
-            if world > 1:
-                t = torch.tensor([tms], device=dev)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                tms = float(t.item())
-            tpf[f"m{mt}"] = {"us_per_step": round(tms * 1e3, 2), "weight_gbs": round(wbytes / (tms / 1e3) / 1e9, 2)}
+            tms = max_over_ranks(e0.elapsed_time(e1) / (it * reps_f))
+            rec = {"us_per_step": round(tms * 1e3, 2), "weight_gbs": round(wbytes / (tms / 1e3) / 1e9, 2)}
+            if mt >= 2048:
+                rec["tflops"] = round(6.0 * mt * hid * inter / (tms / 1e3) / 1e12, 2)
+            tpf[f"m{mt}"] = rec
+            del fg
         del ffn
 
     cpu = None
@@ -598,12 +691,14 @@ def run_ours(args, rank: int, world: int) -> None:
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": steps,
             "timed_repeats": repeats,
             "warmup": args.warmup, "ms_per_step": round(ms / steps, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u4 x bf16 -> fp32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "u4 x bf16 -> fp32", "data": "synthetic",
             "config": {"workload": "q4k_llama3_8b_layer_decode_m1", "m": 1, "qtype": "Q4_K",
                        "projections": {nm: [k, n] for nm, n, k in LAYER},
                        "weight_bytes_per_step": sum(n * k // 256 * 144 for _, n, k in LAYER),
                        "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
-                       "graph": "CUDA graphs of 30 consecutive steps (+ one of the remainder), K steps per timed region, median of the repeated regions", "launches_per_step": [g[0] for g in GROUPS], "parallelism": f"dp{world} (independent layer per rank)"},
+                       "graph": "CUDA graphs of 30 consecutive steps (+ one of the remainder), K steps per timed region, median of the repeated regions", "launches_per_step": [g[0] for g in GROUPS],
+                       "parallelism": (f"tp{world}: q/k/v and gate/up split by output rows, o and down by input "
+                                       f"columns, 2 NCCL all-reduces per step" if world > 1 else "tp1")},
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": "gemv_i8_kernel<Q4_K>", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -612,8 +707,11 @@ def run_ours(args, rank: int, world: int) -> None:
                          "per_launch_frac": per_frac},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "breakdown": e2e_parts,
-                    "path": "LlamaB200Model.layer_linears_graph (one CUDA-graph replay per step holding the packed H2D copy from pinned host memory, the projections and the packed D2H copy), and a host wait per step"},
+                    "path": ("LlamaB200Model.layer_linears_graph" if world == 1 else "TensorParallelLayerLinears.graph_step")
+                    + " (one CUDA-graph replay per step holding the packed H2D copy from pinned host memory, the "
+                      "projections and the packed D2H copy), and a host wait per step"},
             "gpu_launches": len(GROUPS) * steps * repeats,
+            "comm": comm,
             "clocks": clocks,
             "prefill": pre,
             "prefill_sweep": prefill_sweep,
