@@ -261,6 +261,35 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k,
                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * GEMM (any M) with the FFN epilogues, the batched-decode / prefill counterparts of
+ * ggufmm_gemv_swiglu and ggufmm_gemv_residual:
+ *   ggufmm_gemm_swiglu:   y = silu(x Wg^T) * (x Wu^T)  (gate and up of one qtype, N, K)
+ *   ggufmm_gemm_residual: y = x W^T + resid            (resid in y's dtype, stride ldr, may be y)
+ * replacing the reference's gate/up dispatches + gelu_mul shader
+ * (vllm_webgpu/models/llama.py:343-352, shaders/generic/gelu_mul.wgsl:14-20) and the
+ * o / down dispatch + add shader (llama.py:329-335, 355-363). The GEMM leaves fp32
+ * partial sums in the workspace (Q4_K at M <= 128: the fused-dequant kernel, one launch
+ * for gate and up; otherwise dequantize + tcgen05 GEMM per weight) and one pass sums
+ * them in a fixed order, applies the epilogue in fp32 and rounds once into y.
+ * workspace: ggufmm_gemm_ffn_workspace_size(qtype, M, N, K, swiglu) bytes, 256-byte
+ * aligned. Same argument gate as ggufmm_gemm.
+ */
+size_t ggufmm_gemm_ffn_workspace_size(int qtype, int64_t m, int64_t n, int64_t k, int swiglu);
+/* The epilogue pass alone, over fp32 sums the caller already has (e.g. from a grouped
+ * decode GEMV): swiglu != 0: sums [m, 2n] (gate | up) -> y = silu(gate) * up;
+ * swiglu == 0: sums [m, n] -> y = sums + resid. */
+int ggufmm_ffn_epilogue(const float* sums, int64_t m, int64_t n, int swiglu, const void* resid, int64_t ldr,
+                        void* y, int y_dtype, int64_t ldy, void* stream);
+int ggufmm_gemm_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k,
+                       const void* x, int x_dtype, int64_t m, int64_t ldx,
+                       void* y, int y_dtype, int64_t ldy,
+                       void* workspace, size_t workspace_bytes, void* stream);
+int ggufmm_gemm_residual(const void* q, int qtype, int64_t n, int64_t k,
+                         const void* x, int x_dtype, int64_t m, int64_t ldx,
+                         void* y, int y_dtype, int64_t ldy, const void* resid, int64_t ldr,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * ggufmm_gemm without a caller-provided workspace, for callers that cannot
  * allocate device memory (for example a host whose own pool owns the GPU's
  * memory and offers no allocator across the FFI, or code that must not

@@ -27,6 +27,11 @@ cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int
 cudaError_t launch_gemm_fused_q4k_grouped(int nseg, const void* const* q, const int64_t* n, const void* x16,
                                           int64_t m, int64_t k, void* const* y, int ytype, const int64_t* ldy,
                                           void* part_ws, size_t part_bytes, cudaStream_t st);
+cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const int64_t* n, const void* x16,
+                                           int64_t m, int64_t k, void* part_ws, size_t part_bytes, int* zs_out,
+                                           cudaStream_t st);
+cudaError_t launch_ffn_epilogue(const float* part, int ks, int64_t m, int64_t n, int mode, const void* resid,
+                                int64_t ldr, void* y, int ytype, int64_t ldy, cudaStream_t st);
 cudaError_t gemv_mma_device_error(int* v, int clear, cudaStream_t st);
 bool gemv_mma_supported(int qtype, int64_t n, int64_t k, int m, int xtype);
 cudaError_t launch_gemv_mma_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -441,6 +446,93 @@ int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qt
     e = launch_gemm_fused_q4k_grouped(nseg, q, n, workspace, m, k, y, y_dtype, ldy,
                                       static_cast<uint8_t*>(workspace) + x16_bytes, workspace_bytes - x16_bytes, st);
   return cuda_status(e);
+}
+
+// ---- GEMM with the FFN epilogues (SwiGLU of gate and up, residual add) ----------------
+// Workspace: [x cast to fp16][fp32 partials, up to 4 K slices x m x (2n | n)][one fp16
+// dequantized weight for the two-pass path].
+static size_t ffn_x16_bytes(int64_t m, int64_t k) { return round256(static_cast<size_t>(m) * k * 2); }
+static size_t ffn_part_bytes(int64_t m, int64_t ntot) { return round256(static_cast<size_t>(4) * m * ntot * 4); }
+
+size_t ggufmm_gemm_ffn_workspace_size(int qtype, int64_t m, int64_t n, int64_t k, int swiglu) {
+  if (!block_of(qtype) || m <= 0 || n <= 0 || k <= 0 || k % block_of(qtype)) return 0;
+  const int64_t ntot = swiglu ? 2 * n : n;
+  return ffn_x16_bytes(m, k) + ffn_part_bytes(m, ntot) + round256(static_cast<size_t>(n) * k * 2);
+}
+
+// gate / up (nseg 2, SwiGLU) or one weight (residual): the GEMM into fp32 partials,
+// then the epilogue pass into y.
+static int gemm_ffn(int nseg, const void* const* qs, int qtype, int64_t n, int64_t k, const void* x, int x_dtype,
+                    int64_t m, int64_t ldx, void* y, int y_dtype, int64_t ldy, const void* resid, int64_t ldr,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  const size_t need = ggufmm_gemm_ffn_workspace_size(qtype, m, n, k, nseg == 2);
+  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(y, elem_size(y_dtype)) || !aligned(x, elem_size(x_dtype)))
+    return GGUFMM_ERR_ALIGN;
+  for (int i = 0; i < nseg; ++i)
+    if (!aligned(qs[i], 2)) return GGUFMM_ERR_ALIGN;
+  if (resid && !aligned(resid, elem_size(y_dtype))) return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ntot = nseg * n;
+  uint8_t* x16 = static_cast<uint8_t*>(workspace);
+  uint8_t* part = x16 + ffn_x16_bytes(m, k);
+  const size_t part_bytes = ffn_part_bytes(m, ntot);
+  uint8_t* w16 = part + part_bytes;
+  cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
+  int zs = 1;
+  bool fused = qtype == kQ4_K && m <= 128 && fused_gemm_enabled();
+  for (int i = 0; i < nseg; ++i) fused = fused && aligned(qs[i], 16);
+  if (e == cudaSuccess && fused) {
+    const int64_t ns[2] = {n, n};
+    e = launch_gemm_fused_q4k_partials(nseg, qs, ns, x16, m, k, part, part_bytes, &zs, st);
+  } else {
+    for (int i = 0; i < nseg && e == cudaSuccess; ++i) {  // dequantize -> fp16, tcgen05 GEMM into fp32 columns
+      e = launch_dequant(qs[i], qtype, n, k, w16, GGUFMM_F16, st);
+      if (e == cudaSuccess)
+        e = launch_gemm_f16(w16, x16, n, m, k, reinterpret_cast<float*>(part) + i * n, GGUFMM_F32, ntot, st);
+    }
+  }
+  if (e == cudaSuccess)
+    e = launch_ffn_epilogue(reinterpret_cast<const float*>(part), zs, m, n, nseg == 2 ? 0 : 1, resid, ldr, y, y_dtype,
+                            ldy, st);
+  return cuda_status(e);
+}
+
+int ggufmm_ffn_epilogue(const float* sums, int64_t m, int64_t n, int swiglu, const void* resid, int64_t ldr, void* y,
+                        int y_dtype, int64_t ldy, void* stream) {
+  if (!sums || !y || (!swiglu && !resid)) return GGUFMM_ERR_ARG;
+  if (!elem_size(y_dtype)) return GGUFMM_ERR_DTYPE;
+  if (m <= 0 || n <= 0 || ldy < n || (!swiglu && ldr < n)) return GGUFMM_ERR_SHAPE;
+  if (!aligned(sums, 4) || !aligned(y, elem_size(y_dtype)) || (resid && !aligned(resid, elem_size(y_dtype))))
+    return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  return cuda_status(launch_ffn_epilogue(sums, 1, m, n, swiglu ? 0 : 1, resid, ldr, y, y_dtype, ldy,
+                                         static_cast<cudaStream_t>(stream)));
+}
+
+int ggufmm_gemm_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k, const void* x,
+                       int x_dtype, int64_t m, int64_t ldx, void* y, int y_dtype, int64_t ldy, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int s = check_matmul_args(q_gate, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (!q_up) return GGUFMM_ERR_ARG;
+  const void* qs[2] = {q_gate, q_up};
+  return gemm_ffn(2, qs, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, nullptr, 0, workspace, workspace_bytes,
+                  stream);
+}
+
+int ggufmm_gemm_residual(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                         int64_t ldx, void* y, int y_dtype, int64_t ldy, const void* resid, int64_t ldr,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
+  if (s) return s;
+  if (!resid) return GGUFMM_ERR_ARG;
+  if (ldr < n) return GGUFMM_ERR_SHAPE;
+  return gemm_ffn(1, &q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, resid, ldr, workspace, workspace_bytes,
+                  stream);
 }
 
 int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,

@@ -280,291 +280,6 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   }
 }
 
-// ---- Q4_K GEMM on the exact products sc*q ----------------------------------
-//
-// Y[m, n] = sum_sb d[n,sb] * sum_{k in sb} (sc q)[n,k] x[m,k]
-//         - sum_sb dmin[n,sb] * sum_j m[n,sb,j] * xs[m,sb,j]
-// (Q4_K: w = d*sc_j*q - dmin*m_j; xs = the sum of x over sub-block j). The A
-// operand of the main MMA is sc*q <= 945, exact in fp16, made with one byte
-// permute, one mask and one hfma2 per two weights ((1024 + q) * sc - 1024 * sc is
-// exact in one fused rounding); each superblock (2 k-blocks) accumulates into its
-// own TMEM buffer, and a second MMA (K = 16: the 8 sub-blocks' m_j, each twice,
-// against the x sums split hi + lo in fp16) gives the min term. The 4 epilogue
-// warps read both buffers once per superblock and form d*acc_q - dmin*acc_m in
-// fp32 registers (one row per thread), double-buffered against the MMAs.
-// Precision: x is fp16 as in the other GEMM paths; the weights enter exactly.
-template <int BN>
-struct ScqSmem {
-  static constexpr uint32_t kA = kTileW * kFKB * 2;
-  static constexpr uint32_t kB = BN * kFKB * 2;
-  static constexpr uint32_t kHdr = kTileW * 16;
-  static constexpr uint32_t kQs = kTileW * 64;
-  static constexpr uint32_t kStage = kA + kB + kHdr + kQs;
-  static constexpr uint32_t kAmin = kTileW * 32;  // 128 rows x 16 fp16, no-swizzle core matrices
-  static constexpr uint32_t kBmin = BN * 32;
-  static constexpr uint32_t kExtra = 2 * kAmin + 2 * kBmin;
-  static constexpr int kStages = (224 * 1024 - kExtra) / kStage < 4 ? (224 * 1024 - kExtra) / kStage : 4;
-  static constexpr uint32_t kAminOff = kStages * kStage;
-  static constexpr uint32_t kBminOff = kAminOff + 2 * kAmin;
-  static constexpr uint32_t kBarOff = kBminOff + 2 * kBmin;
-  static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 4) * 8 + 16 + 1024;
-};
-
-// K-major, no swizzle: 8-row x 16-byte core matrices, the two K halves (16 B
-// each) 128 B apart, consecutive 8-row groups 256 B apart.
-__device__ __forceinline__ uint64_t umma_smem_desc_interleave(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(128 >> 4) << 16;  // leading byte offset: K direction
-  d |= static_cast<uint64_t>(256 >> 4) << 32;  // stride byte offset: 8-row groups
-  d |= static_cast<uint64_t>(1) << 46;         // descriptor version (sm_100)
-  return d;                                    // layout type 0: no swizzle
-}
-
-__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
-  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b),
-                      *reinterpret_cast<__half2*>(&c));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-
-template <int BN>
-__global__ void __launch_bounds__(kFusedThreads(8), 1)
-    gemm_scq_q4k_kernel(const __grid_constant__ FusedSegs sg, const __grid_constant__ CUtensorMap tm_x,
-                        const uint8_t* __restrict__ xs, int mpad, int ytype, int m, int k,
-                        float* __restrict__ part, int kb_per) {
-  using L = ScqSmem<BN>;
-  constexpr int S = L::kStages;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* afull = full + S;
-  uint64_t* empty = afull + S;
-  uint64_t* sbdone = empty + S;  // [2]: a superblock's accumulators are complete
-  uint64_t* sbfree = sbdone + 2;  // [2]: the epilogue has read them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sbfree + 2);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int seg = 0;
-  while (seg + 1 < sg.nseg && static_cast<int>(blockIdx.y) >= sg.tile0[seg + 1]) ++seg;
-  const int m0 = blockIdx.x * BN, n0 = (static_cast<int>(blockIdx.y) - sg.tile0[seg]) * kTileW;
-  const int n = sg.n[seg];
-  const int kb0 = blockIdx.z * kb_per;               // even: slices hold whole superblocks
-  const int nkb = min(k / kFKB - kb0, kb_per);        // even, >= 2
-  const int nsb = nkb >> 1;
-  constexpr uint32_t kCols = 4 * BN;                  // acc_q[2], acc_m[2]
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&afull[s], 8);
-      mbar_init(&empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sbdone[b], 1);
-      mbar_init(&sbfree[b], 4);
-    }
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem_d = *tmem_slot;
-
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S, kb = kb0 + i;
-        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
-        uint8_t* st = smem + s * L::kStage;
-        const int sb = kb >> 1, h = kb & 1;
-        mbar_arrive_expect_tx(&full[s], L::kB + L::kHdr + L::kQs + (h ? L::kBmin : 0u));
-        tma_load_2d(st + L::kA + L::kB, &sg.hdr[seg], 144 * sb, n0, &full[s]);
-        tma_load_2d(st + L::kA + L::kB + L::kHdr, &sg.qs[seg], 144 * sb + 16 + 64 * h, n0, &full[s]);
-        tma_load_2d(st + L::kA, &tm_x, kb * kFKB, m0, &full[s]);
-        tma_load_2d(st + L::kA + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
-        if (h)  // this superblock's x sums, already in the core-matrix order of the min MMA's B
-          bulk_g2s(smem + L::kBminOff + ((i >> 1) & 1) * L::kBmin,
-                   xs + (static_cast<int64_t>(sb) * mpad + m0) * 32, L::kBmin, &full[s]);
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16<BN>();
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % S, sbl = i >> 1, buf = sbl & 1, h = i & 1;
-        const uint32_t par = (i / S) & 1;
-        if (!h && sbl >= 2 && !mbar_wait(&sbfree[buf], ((sbl >> 1) - 1) & 1)) break;
-        if (!mbar_wait(&full[s], par) || !mbar_wait(&afull[s], par)) break;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc_q = tmem_d + buf * BN, acc_m = tmem_d + (2 + buf) * BN;
-        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
-        const uint32_t b_addr = a_addr + L::kA;
-#pragma unroll
-        for (int atom = 0; atom < 2; ++atom) {
-          const uint64_t adesc = umma_smem_desc(a_addr + atom * (kTileW * 128));
-          const uint64_t bdesc = umma_smem_desc(b_addr + atom * (BN * 128));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_f16(acc_q, adesc + 2 * kk, bdesc + 2 * kk, idesc, (h > 0 || atom > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (h) {  // min term of the superblock: one K = 16 MMA
-          umma_f16(acc_m, umma_smem_desc_interleave(smem_u32(smem + L::kAminOff + buf * L::kAmin)),
-                   umma_smem_desc_interleave(smem_u32(smem + L::kBminOff + buf * L::kBmin)), idesc, 0u);
-        }
-        umma_commit(&empty[s]);
-        if (h) umma_commit(&sbdone[buf]);
-      }
-    }
-  } else if (warp < 6) {
-    // ---------------- epilogue: per-superblock scaling, one weight row per thread ----------------
-    const int quad = warp & 3;
-    const int nrow = n0 + quad * 32 + lane;
-    const bool row_ok = nrow < n;
-    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint8_t* hrow = sg.q[seg] + static_cast<int64_t>(row_ok ? nrow : 0) * sg.row_bytes;
-    float acc[BN];
-#pragma unroll
-    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
-    uint32_t dd = row_ok ? __ldg(reinterpret_cast<const unsigned int*>(hrow + 144 * (kb0 >> 1))) : 0u;
-    bool ok = true;
-    for (int sbl = 0; sbl < nsb; ++sbl) {
-      const int buf = sbl & 1;
-      const uint32_t dd_next = (row_ok && sbl + 1 < nsb)
-                                   ? __ldg(reinterpret_cast<const unsigned int*>(hrow + 144 * ((kb0 >> 1) + sbl + 1)))
-                                   : 0u;
-      const float d = half_bits_to_float(dd), ndmin = -half_bits_to_float(dd >> 16);
-      if (!mbar_wait(&sbdone[buf], (sbl >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t rq[16], rm[16];
-        tmem_ld16(tmem_d + lane_off + buf * BN + c0, rq);
-        tmem_ld16(tmem_d + lane_off + (2 + buf) * BN + c0, rm);
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          acc[c0 + j] = fmaf(ndmin, __uint_as_float(rm[j]), fmaf(d, __uint_as_float(rq[j]), acc[c0 + j]));
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sbfree[buf]);
-      dd = dd_next;
-    }
-    if (ok && row_ok) {
-      void* const y = sg.y[seg];
-      const int64_t ldy = sg.ldy[seg];
-      const int64_t ntot = sg.row0[sg.nseg], grow = sg.row0[seg] + nrow;
-#pragma unroll
-      for (int j = 0; j < BN; ++j) {
-        const int mm = m0 + j;
-        if (mm >= m) continue;
-        if (part)
-          part[(static_cast<int64_t>(blockIdx.z) * m + mm) * ntot + grow] = acc[j];
-        else
-          store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, acc[j]);
-      }
-    }
-  } else {
-    // ---------------- producers of the exact sc*q operand ----------------
-    const int dt = (warp - 6) * 32 + lane;
-    const int r = dt & (kTileW - 1), q = dt >> 7;  // row, 64-weight half of the k-block
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % S, kb = kb0 + i;
-      if (!mbar_wait(&full[s], (i / S) & 1)) break;
-      uint8_t* st = smem + s * L::kStage;
-      const uint4 hd = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + r * 16);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + L::kHdr + r * 64 + q * 32 + 16);
-      const int c = 2 * (kb & 1) + q;  // nibble chunk: low nibbles = sub-block 2c, high = 2c+1
-      const uint32_t hi_sel = 0u - static_cast<uint32_t>(c >> 1);
-      const uint32_t scw = ((hd.y & 0x3F3F3F3Fu) & ~hi_sel) | (((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) & hi_sel);
-      const uint32_t sh = 16u * (c & 1);
-      const uint32_t sc_lo = (scw >> sh) & 0xFFu, sc_hi = (scw >> (sh + 8)) & 0xFFu;
-      // half2 (sc, sc) and (-1024 sc, -1024 sc): integers below 2^16, exact in fp16
-      const __half h_lo = __ushort2half_rn(static_cast<unsigned short>(sc_lo));
-      const __half h_hi = __ushort2half_rn(static_cast<unsigned short>(sc_hi));
-      const __half2 s2lo = __halves2half2(h_lo, h_lo), s2hi = __halves2half2(h_hi, h_hi);
-      const __half2 c2lo = __hmul2(s2lo, __float2half2_rn(-1024.f)), c2hi = __hmul2(s2hi, __float2half2_rn(-1024.f));
-      const uint32_t slo = *reinterpret_cast<const uint32_t*>(&s2lo), shi = *reinterpret_cast<const uint32_t*>(&s2hi);
-      const uint32_t clo = *reinterpret_cast<const uint32_t*>(&c2lo), chi = *reinterpret_cast<const uint32_t*>(&c2hi);
-      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-      uint8_t* arow = st + q * (kTileW * 128) + r * 128;  // atom q, row r
-#pragma unroll
-      for (int kc = 0; kc < 4; ++kc) {  // bytes 8kc..8kc+7: k 8kc.. (low nibbles) and 32 + 8kc.. (high)
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t src = w[2 * kc + (e >> 1)];
-          // two bytes -> two fp16 lanes 0x64XY (1024 + byte): then the low or high nibble
-          const uint32_t t = __byte_perm(src, 0x6464u, (e & 1) ? 0x5342u : 0x5140u);
-          lo[e] = hfma2_u32(t & 0xFF0FFF0Fu, slo, clo);
-          hi[e] = hfma2_u32(((t >> 4) & 0x000F000Fu) | 0x64006400u, shi, chi);
-        }
-        *reinterpret_cast<uint4*>(arow + ((kc ^ (r & 7)) << 4)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(arow + (((kc + 4) ^ (r & 7)) << 4)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      }
-      if (kb & 1) {
-        // min-term A: row r, k = 2j and 2j + 1 both m_j (6-bit, exact); this thread
-        // writes sub-blocks 4q..4q+3 (K half q of the core-matrix layout)
-        const uint32_t mw = q == 0 ? (hd.z & 0x3F3F3F3Fu) : (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u));
-        uint32_t mv[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __half hm = __ushort2half_rn(static_cast<unsigned short>((mw >> (8 * e)) & 0xFFu));
-          const __half2 h2 = __halves2half2(hm, hm);
-          mv[e] = *reinterpret_cast<const uint32_t*>(&h2);
-        }
-        *reinterpret_cast<uint4*>(smem + L::kAminOff + ((i >> 1) & 1) * L::kAmin + (r >> 3) * 256 + q * 128 +
-                                  (r & 7) * 16) = make_uint4(mv[0], mv[1], mv[2], mv[3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[s]);
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (warp == 1) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kCols) : "memory");
-  }
-}
-
-// x sums for the min MMA's B operand: per superblock and token, the 8 sub-block
-// sums of the fp16 activations split into fp16 hi + lo (k = 2j, 2j + 1), stored
-// as [superblock][token / 8][K half (sub-blocks 0-3 | 4-7)][token % 8][8 fp16]
-// so that BN consecutive tokens are one contiguous core-matrix block; tokens
-// m..mpad-1 are zero.
-__global__ void xsum_q4k_kernel(const __half* __restrict__ x16, int m, int mpad, int k, uint8_t* __restrict__ xs) {
-  const int nsb = k / 256;
-  const int64_t total = static_cast<int64_t>(nsb) * mpad * 8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int j = static_cast<int>(i & 7), t = static_cast<int>((i >> 3) % mpad), sb = static_cast<int>((i >> 3) / mpad);
-    float sum = 0.f;
-    if (t < m) {
-      const __half* p = x16 + static_cast<int64_t>(t) * k + sb * 256 + 32 * j;
-      for (int e = 0; e < 32; ++e) sum += __half2float(p[e]);
-    }
-    const __half hi = __float2half_rn(sum);
-    const __half lo = __float2half_rn(sum - __half2float(hi));
-    __half* o = reinterpret_cast<__half*>(xs + (static_cast<int64_t>(sb) * mpad + (t & ~7)) * 32 + (j >> 2) * 128 +
-                                          (t & 7) * 16 + (j & 3) * 4);
-    o[0] = hi;
-    o[1] = lo;
-  }
-}
-
 // ---- host side --------------------------------------------------------------
 // uint8 2-D map over the GGUF bytes [rows, row_bytes], box = box_bytes x 128 rows.
 static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes) {
@@ -656,10 +371,13 @@ static bool fill_segs(FusedSegs& sg, ReduceSegs& rs, int nseg, const void* const
   return true;
 }
 
+// zs_out != nullptr: every K slice (even a single one) leaves its fp32 partials in
+// part_ws and no reduction is launched; *zs_out receives the slice count, for an
+// epilogue pass (ffn_epilogue_kernel) that sums them.
 template <int BN, int DQ, bool X2>
 static cudaError_t launch_fused_bn(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
                                    int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
-                                   size_t part_bytes, cudaStream_t st) {
+                                   size_t part_bytes, cudaStream_t st, int* zs_out = nullptr) {
   using L = FusedSmem<BN>;
   FusedSegs sg;
   ReduceSegs rs;
@@ -683,64 +401,16 @@ static cudaError_t launch_fused_bn(int nseg, const void* const* q, const int64_t
   const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, ntot, part_bytes) : 1;
   const int kb_per = (nkb + ks - 1) / ks;
   const int zs = (nkb + kb_per - 1) / kb_per;  // slices actually used (each >= 1 k-block)
-  float* part = zs > 1 ? static_cast<float*>(part_ws) : nullptr;
+  float* part = (zs > 1 || zs_out) ? static_cast<float*>(part_ws) : nullptr;
+  if (zs_out && (!part || part_bytes < static_cast<size_t>(zs) * m * ntot * 4)) return cudaErrorInvalidValue;
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(zs));
   fn<<<grid, kFusedThreads(DQ), L::kTotal, st>>>(sg, mx, ytype, static_cast<int>(m), static_cast<int>(k), part,
                                                   kb_per);
   e = cudaGetLastError();
-  if (e != cudaSuccess || !part) return e;
-  const int64_t total = m * ntot;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
-  fused_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, zs, static_cast<int>(m), rs, ytype);
-  return cudaGetLastError();
-}
-
-// The sc*q kernel (M <= 64): x sums, the GEMM, and the ordered reduction of its K
-// slices. part_ws holds the x sums first, then the partials.
-template <int BN>
-static cudaError_t launch_scq_bn(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
-                                 int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
-                                 size_t part_bytes, cudaStream_t st) {
-  using L = ScqSmem<BN>;
-  FusedSegs sg;
-  ReduceSegs rs;
-  if (!part_ws || !fill_segs(sg, rs, nseg, q, n, k, y, ldy)) return cudaErrorInvalidValue;
-  CUtensorMap mx;
-  if (!make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
-  const int64_t mt = (m + BN - 1) / BN, nt = sg.tile0[nseg], ntot = sg.row0[nseg];
-  const int mpad = static_cast<int>(mt * BN);
-  const int nsb = static_cast<int>(k / 256);
-  const size_t xs_bytes = (static_cast<size_t>(nsb) * mpad * 32 + 255) / 256 * 256;
-  if (part_bytes < xs_bytes) return cudaErrorInvalidValue;
-  uint8_t* xs = static_cast<uint8_t*>(part_ws);
-  auto fn = gemm_scq_q4k_kernel<BN>;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  {
-    std::lock_guard<std::mutex> lk(g_fused_attr_mu);
-    if (!g_fused_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::kTotal));
-      if (e != cudaSuccess) return e;
-      g_fused_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
-    }
+  if (zs_out) {
+    *zs_out = zs;
+    return e;
   }
-  const int64_t xs_threads = static_cast<int64_t>(nsb) * mpad * 8;
-  xsum_q4k_kernel<<<static_cast<int>(std::min<int64_t>((xs_threads + 255) / 256, 8 * 148)), 256, 0, st>>>(
-      static_cast<const __half*>(x16), static_cast<int>(m), mpad, static_cast<int>(k), xs);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  // K slices of whole superblocks
-  void* pws = xs + xs_bytes;
-  const size_t pbytes = part_bytes - xs_bytes;
-  const int ks = pick_fused_ksplit(mt * nt, 2 * nsb, m, ntot, pbytes);
-  const int sb_per = (nsb + ks - 1) / ks;
-  const int zs = (nsb + sb_per - 1) / sb_per;
-  float* part = zs > 1 ? static_cast<float*>(pws) : nullptr;
-  dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(zs));
-  fn<<<grid, kFusedThreads(8), L::kTotal, st>>>(sg, mx, xs, mpad, ytype, static_cast<int>(m), static_cast<int>(k),
-                                                 part, 2 * sb_per);
-  e = cudaGetLastError();
   if (e != cudaSuccess || !part) return e;
   const int64_t total = m * ntot;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
@@ -755,13 +425,13 @@ static cudaError_t launch_scq_bn(int nseg, const void* const* q, const int64_t* 
 template <int BN>
 static cudaError_t launch_fused_dq(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
                                    int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
-                                   size_t part_bytes, cudaStream_t st) {
+                                   size_t part_bytes, cudaStream_t st, int* zs_out = nullptr) {
   static const int dq = env_int("GGUFMM_FUSED_DQ", 8);
   static const int x2 = env_int("GGUFMM_FUSED_F32X2", 1);
   if (dq == 16)
-    return launch_fused_bn<BN, 16, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  return x2 ? launch_fused_bn<BN, 8, true>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st)
-            : launch_fused_bn<BN, 8, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+    return launch_fused_bn<BN, 16, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
+  return x2 ? launch_fused_bn<BN, 8, true>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out)
+            : launch_fused_bn<BN, 8, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
 }
 
 // nseg (1..4) Q4_K weights q[i] (16-byte aligned GGUF blocks [n[i], k/256*144]) times
@@ -772,13 +442,65 @@ cudaError_t launch_gemm_fused_q4k_grouped(int nseg, const void* const* q, const 
                                           int64_t m, int64_t k, void* const* y, int ytype, const int64_t* ldy,
                                           void* part_ws, size_t part_bytes, cudaStream_t st) {
   if (nseg < 1 || nseg > kMaxFusedSegs) return cudaErrorInvalidValue;
-  // GGUFMM_FUSED_SCQ=1: the exact sc*q operand kernel for M <= 64 (experimental)
-  static const int scq = env_int("GGUFMM_FUSED_SCQ", 0);
-  if (scq == 1 && m <= 32) return launch_scq_bn<32>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  if (scq == 1 && m <= 64) return launch_scq_bn<64>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
   if (m <= 32) return launch_fused_dq<32>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
   if (m <= 64) return launch_fused_dq<64>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
   return launch_fused_dq<128>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+}
+
+// The fused GEMM leaving fp32 partials [zs][m][sum of n] in part_ws for an epilogue
+// pass (m <= 128); *zs_out = the K slices.
+cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const int64_t* n, const void* x16,
+                                           int64_t m, int64_t k, void* part_ws, size_t part_bytes, int* zs_out,
+                                           cudaStream_t st) {
+  if (nseg < 1 || nseg > kMaxFusedSegs || m > 128) return cudaErrorInvalidValue;
+  void* ys[kMaxFusedSegs] = {};
+  int64_t lds[kMaxFusedSegs] = {};
+  for (int i = 0; i < nseg; ++i) {
+    ys[i] = part_ws;  // unused: every slice writes partials
+    lds[i] = n[i];
+  }
+  if (m <= 32) return launch_fused_dq<32>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
+  if (m <= 64) return launch_fused_dq<64>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
+  return launch_fused_dq<128>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
+}
+
+// The FFN epilogues, over fp32 partial sums part[ks][m][ntot] (ks K slices summed in
+// order, so the result does not depend on CTA timing):
+//   mode 0 (SwiGLU): ntot = 2n, gate in columns [0, n), up in [n, 2n):
+//            y[mm, r] = silu(g) * u with silu(g) = g / (1 + e^-g) in fp32 -- the reference's
+//            gelu_mul shader (shaders/generic/gelu_mul.wgsl:14-20);
+//   mode 1 (residual): ntot = n, y[mm, r] = sum + resid[mm, r] (resid in y's dtype, row
+//            stride ldr; it may be y itself) -- the reference's add shader after the o / down
+//            projection (models/llama.py:335, 362).
+// One rounding into y's dtype.
+__global__ void ffn_epilogue_kernel(const float* __restrict__ part, int ks, int m, int n, int mode, const void* resid,
+                                    int64_t ldr, void* y, int ytype, int64_t ldy) {
+  const int64_t ntot = mode == 0 ? 2 * static_cast<int64_t>(n) : n;
+  const int64_t total = static_cast<int64_t>(m) * n, slice = static_cast<int64_t>(m) * ntot;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t mm = i / n, r = i - mm * n;
+    float a = 0.f;
+    for (int z = 0; z < ks; ++z) a += part[z * slice + mm * ntot + r];
+    float v;
+    if (mode == 0) {
+      float u = 0.f;
+      for (int z = 0; z < ks; ++z) u += part[z * slice + mm * ntot + n + r];
+      v = a / (1.f + __expf(-a)) * u;
+    } else {
+      v = a + load_y_rt(resid, ytype, mm * ldr + r);
+    }
+    store_y_rt(y, ytype, mm * ldy + r, v);
+  }
+}
+
+cudaError_t launch_ffn_epilogue(const float* part, int ks, int64_t m, int64_t n, int mode, const void* resid,
+                                int64_t ldr, void* y, int ytype, int64_t ldy, cudaStream_t st) {
+  const int64_t total = m * n;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
+  ffn_epilogue_kernel<<<blocks, 256, 0, st>>>(part, ks, static_cast<int>(m), static_cast<int>(n), mode, resid, ldr, y,
+                                              ytype, ldy);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,

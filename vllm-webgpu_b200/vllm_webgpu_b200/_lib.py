@@ -52,6 +52,10 @@ SIGNATURES = {
     "ggufmm_gemm_workspace_size": (_SZ, [_I, _I64, _I64, _I64]),
     "ggufmm_gemm": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
     "ggufmm_mul_mat": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
+    "ggufmm_gemm_ffn_workspace_size": (_SZ, [_I, _I64, _I64, _I64, _I]),
+    "ggufmm_ffn_epilogue": (_I, [_VP, _I64, _I64, _I, _VP, _I64, _VP, _I, _I64, _VP]),
+    "ggufmm_gemm_swiglu": (_I, [_VP, _VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
+    "ggufmm_gemm_residual": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _I64, _VP, _SZ, _VP]),
     "ggufmm_gemm_noalloc": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
 }
 

@@ -72,21 +72,16 @@ class LlamaB200Model(BaseB200Model):
 
     def _linear_residual(self, x: torch.Tensor, w, out: torch.Tensor, residual):
         """out = x W^T (+ residual): the reference's projection followed by its add
-        shader (llama.py:329-335, 357-363). Decode on the integer GEMV adds the
-        residual in the GEMV's epilogue (one launch, rounded once); otherwise the
-        projection is followed by an elementwise add."""
+        shader (llama.py:329-335, 357-363), here one native call: the decode GEMV with
+        the add in its epilogue, or the GEMM with the add in its epilogue pass (the sum
+        rounded once). ``out`` may be ``residual`` (h = h + proj in place)."""
         if residual is None:
             return self._linear(x, w, out)
-        if isinstance(w, GGUFQuantTensor) and ops.residual_fusable(x, w) and out.dtype == residual.dtype:
-            try:
-                ops.gemv_residual(x, w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
-                return out
-            except ValueError as exc:
-                if not _lib.is_align_refusal(exc):
-                    raise
-                # misaligned operands, which the fused GEMV refuses: projection, then the add
+        if isinstance(w, GGUFQuantTensor) and out.dtype == residual.dtype and x.is_cuda:
+            ops.linear_residual(x.reshape(-1, w.k), w, residual.reshape(-1, w.n), out=out.reshape(-1, w.n))
+            return out
+        # dense (USE_QUANT=0) weights
         if out.data_ptr() == residual.data_ptr() or _overlaps(out, residual):
-            # h = h + proj in place: project into a temporary so the residual survives
             tmp = torch.empty_like(out)
             self._linear(x, w, tmp)
             torch.add(tmp, residual, out=out)
@@ -109,23 +104,17 @@ class LlamaB200Model(BaseB200Model):
         return self._linear_residual(ffn_act, self._w(layer, "down"), out, residual)
 
     def project_ffn_act(self, layer: int, ffn_normed: torch.Tensor, act_buf: torch.Tensor) -> torch.Tensor:
-        """The FFN activation silu(gate) * up into ``act_buf``: in decode one fused
-        launch (ggufmm_gemv_swiglu), where the reference runs the gate and up
-        dispatches and its gelu_mul SwiGLU shader (llama.py:343-352); otherwise the
-        two projections and the activation separately."""
+        """The FFN activation silu(gate) * up into ``act_buf``, where the reference runs
+        the gate and up dispatches and its gelu_mul SwiGLU shader (llama.py:343-352):
+        one native call -- the fused decode GEMV (M <= 8) or the GEMM with the SwiGLU in
+        its epilogue pass."""
         gate, up = self._w(layer, "gate"), self._w(layer, "up")
-        if (isinstance(gate, GGUFQuantTensor) and isinstance(up, GGUFQuantTensor)
-                and ops.swiglu_fusable(ffn_normed, gate, up)):
-            try:
-                return ops.gemv_swiglu(ffn_normed, gate, up, out=act_buf.reshape(-1, gate.n))
-            except ValueError as exc:
-                if not _lib.is_align_refusal(exc):
-                    raise
-                # misaligned operands: the two projections and the activation separately
+        if isinstance(gate, GGUFQuantTensor) and isinstance(up, GGUFQuantTensor) and gate.qtype == up.qtype:
+            return ops.swiglu(ffn_normed, gate, up, out=act_buf.reshape(-1, gate.n))
         g = torch.empty_like(act_buf, dtype=torch.float32)
         u = torch.empty_like(act_buf, dtype=torch.float32)
         self.project_gate_up(layer, ffn_normed, g, u)
-        act_buf.copy_(torch.nn.functional.silu(g) * u)
+        act_buf.copy_(torch.nn.functional.silu(g) * u)  # dense (USE_QUANT=0) weights
         return act_buf
 
     def embed_tokens(self, input_ids: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

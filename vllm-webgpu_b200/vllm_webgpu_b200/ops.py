@@ -226,6 +226,118 @@ def gemv_residual(x: torch.Tensor, w: GGUFQuantTensor, residual: torch.Tensor,
     return y
 
 
+_ffn_workspaces: dict = {}
+
+
+def _ffn_workspace(w: GGUFQuantTensor, m: int, swiglu: bool) -> torch.Tensor:
+    need = int(_lib.lib().ggufmm_gemm_ffn_workspace_size(w.qtype, m, w.n, w.k, int(swiglu)))
+    idx = w.data.device.index
+    ws = _ffn_workspaces.get(idx)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(max(need, 256), dtype=torch.uint8, device=w.data.device)
+        _ffn_workspaces[idx] = ws
+    return ws
+
+
+def gemm_swiglu(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """out = silu(x gate^T) * (x up^T) at any M through the tensor-core GEMM with the
+    SwiGLU in its epilogue pass (ggufmm_gemm_swiglu), replacing the reference's gate and
+    up dispatches and its gelu_mul shader (vllm_webgpu/models/llama.py:343-352)."""
+    if gate.shape != up.shape or gate.qtype != up.qtype:
+        raise ValueError("gate and up must share shape and quantization type")
+    dev = _require_cuda(x, gate.data, up.data)
+    x2 = _as_2d(x, gate.k)
+    y = _out(x2, gate.n, out, out_dtype)
+    ws = _ffn_workspace(gate, x2.shape[0], True)
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemm_swiglu(gate.data.data_ptr(), up.data.data_ptr(), gate.qtype, gate.n, gate.k,
+                                           x2.data_ptr(), _code(x2.dtype), x2.shape[0], x2.stride(0), y.data_ptr(),
+                                           _code(y.dtype), y.stride(0), ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(st, "ggufmm_gemm_swiglu")
+    return y
+
+
+def gemm_residual(x: torch.Tensor, w: GGUFQuantTensor, residual: torch.Tensor,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = x W^T + residual at any M, the add in the GEMM's epilogue pass
+    (ggufmm_gemm_residual); ``out`` may be ``residual`` (in place)."""
+    dev = _require_cuda(x, w.data, residual)
+    x2 = _as_2d(x, w.k)
+    r2 = residual.reshape(-1, w.n) if residual.dim() != 2 else residual
+    if r2.shape != (x2.shape[0], w.n) or r2.stride(1) != 1:
+        raise ValueError(f"residual must be [{x2.shape[0]}, {w.n}] with unit column stride")
+    y = _out(x2, w.n, out, r2.dtype)
+    if y.dtype != r2.dtype:
+        raise ValueError("out and residual must share a dtype")
+    ws = _ffn_workspace(w, x2.shape[0], False)
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_gemm_residual(w.data.data_ptr(), w.qtype, w.n, w.k, x2.data_ptr(), _code(x2.dtype),
+                                             x2.shape[0], x2.stride(0), y.data_ptr(), _code(y.dtype), y.stride(0),
+                                             r2.data_ptr(), r2.stride(0), ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(st, "ggufmm_gemm_residual")
+    return y
+
+
+def ffn_epilogue(sums: torch.Tensor, n: int, out: torch.Tensor, swiglu: bool,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
+    """The epilogue pass over fp32 sums (ggufmm_ffn_epilogue): swiglu, sums [M, 2n] (gate |
+    up) -> out = silu(gate) * up; else sums [M, n] -> out = sums + residual."""
+    dev = _require_cuda(sums, out)
+    if sums.dtype != torch.float32 or not sums.is_contiguous():
+        raise ValueError("sums must be contiguous float32")
+    m = sums.shape[0]
+    r = residual.reshape(m, n) if residual is not None else None
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_ffn_epilogue(sums.data_ptr(), m, n, int(swiglu), r.data_ptr() if r is not None else None,
+                                            r.stride(0) if r is not None else 0, out.data_ptr(), _code(out.dtype),
+                                            out.stride(0), _stream(dev))
+    _lib.check(st, "ggufmm_ffn_epilogue")
+    return out
+
+
+def swiglu(x: torch.Tensor, gate: GGUFQuantTensor, up: GGUFQuantTensor, out: torch.Tensor | None = None,
+           out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """silu(x gate^T) * (x up^T) on the fastest native path: the one-launch integer decode
+    GEMV where it serves the shape; other decode shapes run the grouped decode GEMV into
+    fp32 sums and the epilogue pass; above the GEMV the GEMM with the SwiGLU epilogue."""
+    x2 = _as_2d(x, gate.k)
+    m = x2.shape[0]
+    if swiglu_fusable(x2, gate, up):
+        try:
+            return gemv_swiglu(x2, gate, up, out=out, out_dtype=out_dtype)
+        except ValueError as exc:
+            if not _lib.is_align_refusal(exc):
+                raise
+    if gemv_preferred(m, gate, x2.dtype) and gate.shape == up.shape and gate.qtype == up.qtype:
+        sums = torch.empty((m, 2 * gate.n), dtype=torch.float32, device=x2.device)
+        gemv_grouped(x2, [gate, up], outs=[sums[:, :gate.n], sums[:, gate.n:]])
+        y = _out(x2, gate.n, out, out_dtype)
+        return ffn_epilogue(sums, gate.n, y, swiglu=True)
+    return gemm_swiglu(x2, gate, up, out=out, out_dtype=out_dtype)
+
+
+def linear_residual(x: torch.Tensor, w: GGUFQuantTensor, residual: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """x W^T + residual on the fastest native path: the integer decode GEMV with the add in
+    its epilogue, other decode shapes as a GEMV into fp32 plus the epilogue pass, above
+    the GEMV the GEMM with the add in its epilogue pass."""
+    x2 = _as_2d(x, w.k)
+    m = x2.shape[0]
+    if residual_fusable(x2, w):
+        try:
+            return gemv_residual(x2, w, residual, out=out)
+        except ValueError as exc:
+            if not _lib.is_align_refusal(exc):
+                raise
+    if gemv_preferred(m, w, x2.dtype):
+        sums = gemv(x2, w, out_dtype=torch.float32)
+        r2 = residual.reshape(m, w.n)
+        y = _out(x2, w.n, out, r2.dtype)
+        return ffn_epilogue(sums, w.n, y, swiglu=False, residual=r2)
+    return gemm_residual(x2, w, residual, out=out)
+
+
 class PeerExchange:
     """Exchange buffers for ``gemv_allreduce`` on every GPU of a process group:
     one symmetric-memory allocation per GPU (``torch.distributed._symmetric_memory``,

@@ -82,38 +82,24 @@ class TensorParallelSwiGLU:
         llama.py:362-363): rank 0 adds it to its partial before the all-reduce, so the
         sum carries it once -- in the down projection's epilogue when that GEMV runs on
         the integer tensor cores with the residual in the reduce dtype."""
-        act = None
         if self.fused_swiglu and x.is_cuda:
             from . import ops
-            if ops.swiglu_fusable(x, self.gate, self.up):
-                # decode: gate, up and SwiGLU in one launch (fp32 activation); shapes whose
-                # activations do not fit the kernel's shared memory are excluded by swiglu_fusable
-                try:
-                    act = ops.gemv_swiglu(x, self.gate, self.up, out_dtype=torch.float32)
-                except ValueError as exc:
-                    if not _lib.is_align_refusal(exc):
-                        raise
-                    act = None
-        if act is None:
+            # gate, up and SwiGLU in one native call (fp32 activation): the decode GEMV or
+            # the GEMM with the SwiGLU epilogue
+            act = ops.swiglu(x, self.gate, self.up, out_dtype=torch.float32)
+        else:
             g = self.matmul(x, self.gate, out_dtype=torch.float32)
             u = self.matmul(x, self.up, out_dtype=torch.float32)
-            act = torch.nn.functional.silu(g) * u  # fp32 SwiGLU, fed to down in fp32
+            act = torch.nn.functional.silu(g) * u  # injected (CPU test) matmul: fp32 SwiGLU
         if self.world > 1 and self.fused_allreduce and act.is_cuda and act.shape[0] <= 8:
             y = self._down_allreduce(act)
             if y is not None:
                 return y if residual is None else y.add_(residual)
-        y = None
         add_here = residual is not None and self.rank == 0
-        if add_here and self.fused_swiglu and residual.dtype == self.reduce_dtype:
+        if add_here and self.fused_swiglu and residual.dtype == self.reduce_dtype and act.is_cuda:
             from . import ops
-            if ops.residual_fusable(act, self.down):
-                try:
-                    y = ops.gemv_residual(act, self.down, residual)
-                except ValueError as exc:
-                    if not _lib.is_align_refusal(exc):
-                        raise
-                    y = None  # misaligned operands the fused GEMV refuses: projection, then the add
-        if y is None:
+            y = ops.linear_residual(act, self.down, residual)  # the add in the GEMV / GEMM epilogue
+        else:
             y = self.matmul(act, self.down, out_dtype=self.reduce_dtype)
             if add_here:
                 y.add_(residual)
