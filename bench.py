@@ -255,7 +255,7 @@ def run_reference(args, rank: int, world: int) -> None:
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(res["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------------
@@ -378,7 +378,9 @@ def run_ours(args, rank: int, world: int) -> None:
         ms_nc = max_over_ranks(statistics.median([timed_run(nb, ns) for _ in range(max(1, repeats // 2))]))
         comm = {"step_us_without_allreduce": round(ms_nc / steps * 1e3, 2),
                 "allreduce_share_of_step": round(max(0.0, 1.0 - ms_nc / ms), 4),
-                "allreduces_per_step": 2, "allreduce_bytes": m * hid * 4, "collective": "NCCL all_reduce (fp32)"}
+                "allreduces_per_step": 2, "allreduce_bytes": m * hid * 4,
+                "collective": ("ggufmm_allreduce (one-shot, NVLink peer memory, fp32)" if tp0.peer_allreduce
+                               else "NCCL all_reduce (fp32)")}
         del nb, ns
 
     # per-launch device time of each launch of the (local) step, each alone in a CUDA
@@ -527,22 +529,33 @@ def run_ours(args, rank: int, world: int) -> None:
                 yp = torch.empty((pm, r1 - r0), dtype=torch.bfloat16, device=dev)
                 yg = torch.empty((world * pm, r1 - r0), dtype=torch.bfloat16, device=dev) if world > 1 else None
 
+                pg = ops.PeerGather(pm, pn, torch.bfloat16, device=dev) if world > 1 else None
+
                 def pstep(gather: bool = True) -> None:
-                    ops.gemm(xp, wts[qt], out=yp)
                     if world > 1 and gather:
-                        dist.all_gather_into_tensor(yg, yp)
+                        # the all-gather in the GEMM's epilogue (peer stores over NVLink) + a device barrier
+                        ops.gemm_allgather(xp, wts[qt], pg)
+                    else:
+                        ops.gemm(xp, wts[qt], out=yp)
+
+                def pstep_nccl() -> None:
+                    ops.gemm(xp, wts[qt], out=yp)
+                    dist.all_gather_into_tensor(yg, yp)
                 for _ in range(3):
                     pstep()
                 torch.cuda.synchronize()
                 it = max(3, int(2e12 / (2.0 * pm * pn * pk)))  # ~10 ms of work at least
 
-                def ptime(gather: bool) -> float:
+                def ptime(gather: bool, fn=None) -> float:
                     if world > 1:
                         dist.barrier()
                     torch.cuda.synchronize()
                     e0.record(stream)
                     for _ in range(it):
-                        pstep(gather)
+                        if fn is not None:
+                            fn()
+                        else:
+                            pstep(gather)
                     e1.record(stream)
                     torch.cuda.synchronize()
                     return max_over_ranks(e0.elapsed_time(e1) / it)
@@ -554,12 +567,15 @@ def run_ours(args, rank: int, world: int) -> None:
                     pms_ng = ptime(False)
                     rec["allgather_share"] = round(max(0.0, 1.0 - pms_ng / pms), 4)
                     rec["ms_without_allgather"] = round(pms_ng, 4)
+                    pstep_nccl()
+                    rec["ms_gemm_then_nccl_allgather"] = round(ptime(True, pstep_nccl), 4)
                 prefill_sweep[f"{qname}_m{pm}"] = rec
-                del xp, yp, yg
+                del xp, yp, yg, pg
         p2 = prefill_sweep["q4_k_m2048"]
         pre = {"workload": "q4k_prefill_m2048_k4096_n14336", **p2,
                "path": ("dequant->fp16 + cast->fp16 workspace, persistent tcgen05 GEMM (3 kernels)"
-                        + ("" if world == 1 else f"; N split over {world} ranks + NCCL all_gather of the outputs"))}
+                        + ("" if world == 1 else f"; N split over {world} ranks, all-gather in the GEMM epilogue "
+                                                 "(peer stores over NVLink) + device barrier"))}
         del wts
 
     # BASELINE configs 1 and 2 on the GPU: Q8_0 4096 x 4096 matvec with fp32 x, and the
@@ -698,7 +714,7 @@ def run_ours(args, rank: int, world: int) -> None:
                        "bytes_per_step": step_bytes, "l2": "3 rotating weight copies (368 MB > 126 MB L2)",
                        "graph": "CUDA graphs of 30 consecutive steps (+ one of the remainder), K steps per timed region, median of the repeated regions", "launches_per_step": [g[0] for g in GROUPS],
                        "parallelism": (f"tp{world}: q/k/v and gate/up split by output rows, o and down by input "
-                                       f"columns, 2 NCCL all-reduces per step" if world > 1 else "tp1")},
+                                       f"columns, 2 all-reduces per step" if world > 1 else "tp1")},
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "kernel": "gemv_i8_kernel<Q4_K>", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -720,7 +736,18 @@ def run_ours(args, rank: int, world: int) -> None:
             "tp_ffn": tpf,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """The one JSON line, on the process's real stdout (libraries' banners -- NCCL's
+    version line among them -- are sent to stderr while the bench runs)."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 
 
 def main() -> None:
@@ -738,6 +765,10 @@ def main() -> None:
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")  # the real stdout, for the JSON line only
+    os.dup2(2, 1)                          # everything else printed on fd 1 goes to stderr
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -240,6 +240,44 @@ int ggufmm_gemv_allreduce(const void* q, int qtype, int64_t n, int64_t k,
                           uint32_t epoch, void* stream);
 
 /*
+ * The N-split prefill GEMM with its all-gather in the epilogue: this GPU's column slice
+ * W [n, K] of a weight split over `world` GPUs; every output value is stored into all
+ * `world` outputs y_peers[i] ([M, ldy], this GPU's and its peers' buffers mapped over
+ * NVLink, e.g. symmetric memory) at column col0 + row, so the gather overlaps the MMAs
+ * of later tiles instead of following the GEMM. Replaces the GEMM followed by an NCCL
+ * all-gather; call ggufmm_peer_barrier afterwards before reading the gathered output.
+ * Dequantize + cast + tcgen05 GEMM (workspace: ggufmm_gemm_workspace_size(qtype, M, n, K)).
+ * The reference has no multi-GPU path.
+ */
+int ggufmm_gemm_allgather(const void* q, int qtype, int64_t n, int64_t k,
+                          const void* x, int x_dtype, int64_t m, int64_t ldx,
+                          void* const* y_peers, int world, int64_t col0, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One-shot all-reduce (sum) of n <= 65536 fp32 values (n a multiple of 4; in, out and
+ * resid 16-byte aligned) over `world` GPUs through NVLink peer memory, for the
+ * tensor-parallel decode step's all-reduces (the o / down partials, M x hidden). Every
+ * GPU of the group calls it with the same n: each stores its input into every GPU's
+ * exchange buffer, raises a per-chunk flag there (generation counters kept in device
+ * memory: the call may be captured in a CUDA graph and replayed), waits (bounded) for
+ * its own flags and writes out = the sum of all ranks' inputs in rank order (+ resid),
+ * the same bits on every GPU. `out` may be `in`.
+ *   peer_bufs  the `world` exchange buffers (valid on this GPU, e.g. symmetric memory
+ *              or CUDA IPC; 256-byte aligned), ggufmm_allreduce_buffer_bytes(n, world) bytes
+ *              each, zero-filled before the first call
+ * A peer that never makes the matching call makes the wait give up (bit 1 of
+ * ggufmm_device_status) and out is left unwritten. The reference has no multi-GPU path.
+ */
+size_t ggufmm_allreduce_buffer_bytes(int64_t n, int world);
+/* The same kernel with no data (exchange buffers of ggufmm_allreduce_buffer_bytes(0,
+ * world) bytes or larger): a barrier across the group's GPUs, after which every rank's earlier work
+ * on its stream -- stores into peers' memory included -- is complete and visible. */
+int ggufmm_peer_barrier(void* const* peer_bufs, int world, int rank, void* stream);
+int ggufmm_allreduce(const float* in, float* out, int64_t n, void* const* peer_bufs, int world, int rank,
+                     const float* resid, void* stream);
+
+/*
  * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
  * arguments). Size it once for the largest M and reuse it.
  */

@@ -132,3 +132,122 @@ def test_tp_ffn_two_gpus_fused_allreduce(cuda, tmp_path):
         x = O.make_activations(m, H, seed=seed)
         xb = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
         assert O.rel_err(a, _oracle_ffn(xb)) <= TOL
+
+
+def _peer_worker(rank, world, port, q):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from vllm_webgpu_b200 import ops
+        n = 4096
+        ar = ops.PeerAllReduce(n, device=torch.device("cuda", rank))
+        outs = []
+        # eager calls, then the same call replayed from a CUDA graph (the generation
+        # counter advances on the device)
+        x = torch.empty(n, dtype=torch.float32, device="cuda")
+        for it in range(3):
+            x.copy_(torch.from_numpy(O.make_activations(1, n, seed=100 * it + rank)).reshape(n))
+            outs.append(ar(x, out=torch.empty_like(x)).cpu().numpy())
+        y = torch.empty_like(x)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g, stream=s):
+            ar(x, out=y)
+        for it in range(3, 6):
+            x.copy_(torch.from_numpy(O.make_activations(1, n, seed=100 * it + rank)).reshape(n))
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            outs.append(y.cpu().numpy())
+        from vllm_webgpu_b200 import _lib
+        q.put((rank, outs, _lib.lib().ggufmm_device_status(1, None)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_two_gpus_eager_and_graph(cuda):
+    """ggufmm_allreduce on 2 GPUs: every rank receives the rank-ordered sum, bit-identical
+    across ranks, eagerly and replayed from a CUDA graph."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_peer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (o, st)) for r, o, st in (q.get(timeout=240) for _ in range(2)))
+    for p in ps:
+        p.join(60)
+    n = 4096
+    for it in range(6):
+        ref = sum(O.make_activations(1, n, seed=100 * it + r).reshape(n).astype(np.float32) for r in range(2))
+        assert np.array_equal(res[0][0][it], res[1][0][it])
+        assert np.allclose(res[0][0][it], ref, rtol=1e-6, atol=1e-6)
+    assert res[0][1] == 0 and res[1][1] == 0
+
+
+def _gather_worker(rank, world, port, q):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from vllm_webgpu_b200 import _lib, ops
+        from vllm_webgpu_b200.formats import GGUFQuantTensor
+        m, n, k = 300, 2048, 1024
+        raw = O.make_weights(n, k, O.Q4_K, seed=77)
+        w = GGUFQuantTensor(torch.from_numpy(raw).cuda(), O.Q4_K, (n, k))
+        r0, r1 = rank * n // world, (rank + 1) * n // world
+        g = ops.PeerGather(m, n, torch.float32, device=torch.device("cuda", rank))
+        outs = []
+        for it in range(2):
+            x = torch.from_numpy(O.make_activations(m, k, seed=5 + it)).to(torch.bfloat16).cuda()
+            y = ops.gemm_allgather(x, w.rows(r0, r1), g)
+            torch.cuda.synchronize()
+            outs.append(y.cpu().numpy().copy())
+        q.put((rank, outs, _lib.lib().ggufmm_device_status(1, None)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gemm_allgather_two_gpus(cuda):
+    """The N-split GEMM with the all-gather in its epilogue: each GPU computes half the
+    output columns and stores them into both GPUs' outputs; after the device barrier
+    both hold the full product (oracle, 2e-3), bit-identical, twice in a row."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (o, st)) for r, o, st in (q.get(timeout=240) for _ in range(2)))
+    for p in ps:
+        p.join(60)
+    m, n, k = 300, 2048, 1024
+    raw = O.make_weights(n, k, O.Q4_K, seed=77)
+    for it in range(2):
+        x = torch.from_numpy(O.make_activations(m, k, seed=5 + it)).to(torch.bfloat16).float().numpy()
+        ref = O.matmul_ref(x, raw, O.Q4_K, n, k)
+        assert np.array_equal(res[0][0][it], res[1][0][it])
+        assert O.rel_err(res[0][0][it], ref) <= TOL
+    assert res[0][1] == 0 and res[1][1] == 0

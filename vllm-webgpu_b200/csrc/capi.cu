@@ -45,6 +45,13 @@ cudaError_t dequant_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t launch_embedding(const void* q, int qtype, int64_t n_vocab, int64_t k, const int32_t* ids, int64_t n_ids,
                              void* out, int out_dtype, int64_t ldo, cudaStream_t st);
 cudaError_t gemv_set_wait_limit(uint32_t polls);
+size_t allreduce_buffer_bytes(int64_t n, int world);
+cudaError_t launch_allreduce_oneshot(const float* in, float* out, int64_t n, void* const* bufs, int world, int rank,
+                                     const void* resid, cudaStream_t st);
+cudaError_t allreduce_device_error(int* v, int clear, cudaStream_t st);
+cudaError_t launch_gemm_f16_peers(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k,
+                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st);
+cudaError_t allreduce_set_wait_limit(uint32_t polls);
 cudaError_t gemm_set_wait_limit(uint32_t polls);
 cudaError_t gemv_mma_set_wait_limit(uint32_t polls);
 cudaError_t gemm_fused_set_wait_limit(uint32_t polls);
@@ -181,8 +188,10 @@ int ggufmm_device_status(int clear, void* stream) {
   if (e == cudaSuccess) e = gemm_fused_device_error(&d, clear, st);
   if (e == cudaSuccess) e = gemv_i8_device_error(&f, clear, st);
   if (e == cudaSuccess) e = dequant_device_error(&h, clear, st);
+  int r = 0;
+  if (e == cudaSuccess) e = allreduce_device_error(&r, clear, st);
   if (e != cudaSuccess) return cuda_status(e);
-  return a | b | c | d | f | h;
+  return a | b | c | d | f | h | r;
 }
 
 int ggufmm_set_wait_limit(uint32_t polls) {
@@ -192,7 +201,35 @@ int ggufmm_set_wait_limit(uint32_t polls) {
   if (e == cudaSuccess) e = gemv_mma_set_wait_limit(v);
   if (e == cudaSuccess) e = gemm_fused_set_wait_limit(v);
   if (e == cudaSuccess) e = gemv_i8_set_wait_limit(v);
+  if (e == cudaSuccess) e = allreduce_set_wait_limit(v);
   return cuda_status(e);
+}
+
+size_t ggufmm_allreduce_buffer_bytes(int64_t n, int world) { return allreduce_buffer_bytes(n, world); }
+
+int ggufmm_allreduce(const float* in, float* out, int64_t n, void* const* peer_bufs, int world, int rank,
+                     const float* resid, void* stream) {
+  if (!in || !out || !peer_bufs) return GGUFMM_ERR_ARG;
+  if (world < 2 || world > 8 || rank < 0 || rank >= world) return GGUFMM_ERR_ARG;
+  if (n <= 0 || !allreduce_buffer_bytes(n, world)) return GGUFMM_ERR_SHAPE;
+  if (!aligned(in, 16) || !aligned(out, 16) || (resid && !aligned(resid, 16))) return GGUFMM_ERR_ALIGN;
+  for (int i = 0; i < world; ++i)
+    if (!peer_bufs[i] || !aligned(peer_bufs[i], 256)) return GGUFMM_ERR_ALIGN;
+  if (!aligned(in, 4) || !aligned(out, 4) || (resid && !aligned(resid, 4))) return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  return cuda_status(launch_allreduce_oneshot(in, out, n, peer_bufs, world, rank, resid,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+int ggufmm_peer_barrier(void* const* peer_bufs, int world, int rank, void* stream) {
+  if (!peer_bufs || world < 2 || world > 8 || rank < 0 || rank >= world) return GGUFMM_ERR_ARG;
+  for (int i = 0; i < world; ++i)
+    if (!peer_bufs[i] || !aligned(peer_bufs[i], 256)) return GGUFMM_ERR_ALIGN;
+  int s = check_device();
+  if (s) return s;
+  return cuda_status(launch_allreduce_oneshot(nullptr, nullptr, 0, peer_bufs, world, rank, nullptr,
+                                              static_cast<cudaStream_t>(stream)));
 }
 
 int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k, void* out, int out_dtype, void* stream) {
@@ -533,6 +570,29 @@ int ggufmm_gemm_residual(const void* q, int qtype, int64_t n, int64_t k, const v
   if (ldr < n) return GGUFMM_ERR_SHAPE;
   return gemm_ffn(1, &q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, resid, ldr, workspace, workspace_bytes,
                   stream);
+}
+
+int ggufmm_gemm_allgather(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,
+                          int64_t ldx, void* const* y_peers, int world, int64_t col0, int y_dtype, int64_t ldy,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!y_peers || world < 1 || world > 8) return GGUFMM_ERR_ARG;
+  int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y_peers[0], y_dtype, ldy);
+  if (s) return s;
+  if (col0 < 0 || col0 + n > ldy) return GGUFMM_ERR_SHAPE;
+  const size_t need = ggufmm_gemm_workspace_size(qtype, m, n, k);
+  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!aligned(q, 2) || !aligned(workspace, 256) || !aligned(x, elem_size(x_dtype))) return GGUFMM_ERR_ALIGN;
+  for (int i = 0; i < world; ++i)
+    if (!y_peers[i] || !aligned(y_peers[i], elem_size(y_dtype))) return GGUFMM_ERR_ALIGN;
+  s = check_device();
+  if (s) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w16 = static_cast<uint8_t*>(workspace);
+  uint8_t* x16 = w16 + round256(static_cast<size_t>(n) * k * 2);
+  cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
+  if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
+  if (e == cudaSuccess) e = launch_gemm_f16_peers(w16, x16, n, m, k, y_peers, world, col0, y_dtype, ldy, st);
+  return cuda_status(e);
 }
 
 int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m,

@@ -31,6 +31,25 @@
 
 namespace ggufmm {
 
+// Optional peer outputs: the tile's values are stored into `world` [m, ldy] outputs
+// (this GPU's and its peers', mapped here over NVLink) at column col0 + row -- the
+// N-split GEMM's all-gather done by the epilogue itself, overlapped with the MMAs of
+// later tiles. world 0: the single output y.
+struct PeerOut {
+  uint64_t y[8];
+  int world;
+  int64_t col0;
+};
+
+__device__ __forceinline__ void store_out(void* y, const PeerOut& po, int ytype, int64_t mm, int64_t ldy, int nrow,
+                                          float v) {
+  if (po.world == 0) {
+    store_y_rt(y, ytype, mm * ldy + nrow, v);
+    return;
+  }
+  for (int p = 0; p < po.world; ++p) store_y_rt(reinterpret_cast<void*>(po.y[p]), ytype, mm * ldy + po.col0 + nrow, v);
+}
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t kABytes = kTileW * kBK * 2;  // 16 KB
@@ -43,7 +62,8 @@ struct GemmSmem {
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                   void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k) {
+                   void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k,
+                              const PeerOut po) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles need 1024-byte aligned bases
@@ -129,7 +149,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int mm = m0 + c0 + j;
-            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+            if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
           }
         }
       }
@@ -152,7 +172,8 @@ __global__ void __launch_bounds__(192, 1)
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                              void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k) {
+                              void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k,
+                              const PeerOut po) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -260,7 +281,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int mm = m0 + c0 + j;
-            if (mm < m) store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+            if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
           }
         }
       }
@@ -283,7 +304,7 @@ static std::set<std::pair<const void*, int>> g_gemm_attr_done;
 
 template <int BN, int STAGES, bool PERSIST = false>
 static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                  int ytype, int64_t ldy, cudaStream_t st) {
+                                  int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po = PeerOut{}) {
   using L = GemmSmem<BN, STAGES>;
   CUtensorMap mw, mx;
   if (!make_map_f16(&mw, w16, n, k, kTileW) || !make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
@@ -307,7 +328,7 @@ static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, i
     grid = dim3(static_cast<unsigned>(std::min<int64_t>(static_cast<int64_t>(grid.x) * grid.y, sms)));
   }
   fn<<<grid, 192, L::kTotal, st>>>(mw, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
-                                   static_cast<int>(k));
+                                   static_cast<int>(k), po);
   return cudaGetLastError();
 }
 
@@ -316,17 +337,34 @@ cudaError_t gemm_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls
 
 // Tensor-core GEMM on fp16 operands already in device memory:
 // w16 [n, k], x16 [m, k] (both row-major, 16-byte aligned, k % 8 == 0).
-cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                            int64_t ldy, cudaStream_t st) {
-  if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
-  if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st);
-  if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st);
+static cudaError_t launch_gemm_f16_po(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
+                                      int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po) {
+  if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+  if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+  if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st, po);
   static const bool persist = [] {
     const char* e = std::getenv("GGUFMM_GEMM_PERSIST");
     return !(e && e[0] == '0');
   }();
-  if (persist) return launch_gemm_bn<256, 4, true>(w16, x16, n, m, k, y, ytype, ldy, st);
-  return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st);
+  if (persist) return launch_gemm_bn<256, 4, true>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+  return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+}
+
+cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
+                            int64_t ldy, cudaStream_t st) {
+  return launch_gemm_f16_po(w16, x16, n, m, k, y, ytype, ldy, st, PeerOut{});
+}
+
+// The same GEMM storing every output value into `world` outputs (all GPUs' [m, ldy]
+// buffers, peers' mapped over NVLink) at column col0 + row.
+cudaError_t launch_gemm_f16_peers(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k,
+                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st) {
+  if (world < 1 || world > 8) return cudaErrorInvalidValue;
+  PeerOut po{};
+  for (int i = 0; i < world; ++i) po.y[i] = reinterpret_cast<uint64_t>(ys[i]);
+  po.world = world;
+  po.col0 = col0;
+  return launch_gemm_f16_po(w16, x16, n, m, k, ys[0], ytype, ldy, st, po);
 }
 
 }  // namespace ggufmm

@@ -49,6 +49,10 @@ SIGNATURES = {
     "ggufmm_gemv_allreduce_buffer_bytes": (_SZ, [_I64, _I64, _I]),
     "ggufmm_gemv_allreduce": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _I, _I, _I64,
                                    ctypes.c_uint32, _VP]),
+    "ggufmm_allreduce_buffer_bytes": (_SZ, [_I64, _I]),
+    "ggufmm_allreduce": (_I, [_VP, _VP, _I64, _VP, _I, _I, _VP, _VP]),
+    "ggufmm_peer_barrier": (_I, [_VP, _I, _I, _VP]),
+    "ggufmm_gemm_allgather": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _I, _I64, _VP, _SZ, _VP]),
     "ggufmm_gemm_workspace_size": (_SZ, [_I, _I64, _I64, _I64]),
     "ggufmm_gemm": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),
     "ggufmm_mul_mat": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP, _SZ, _VP]),

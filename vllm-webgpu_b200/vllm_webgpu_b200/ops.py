@@ -369,6 +369,107 @@ class PeerExchange:
         self.epoch = 0
 
 
+class PeerAllReduce:
+    """One-shot fp32 all-reduce over NVLink peer memory (ggufmm_allreduce) for vectors of
+    up to 65536 values: one symmetric-memory exchange buffer per GPU of the group
+    (``torch.distributed._symmetric_memory``), zero-filled. Creating it is a collective;
+    calls must be made by every rank in the same order, and may be captured in a CUDA
+    graph (the call's generation counter lives in device memory)."""
+
+    MAX_N = 1 << 16
+
+    def __init__(self, n: int, group=None, device: torch.device | None = None):
+        import ctypes
+
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group or dist.group.WORLD
+        self.world, self.rank, self.n = dist.get_world_size(group), dist.get_rank(group), n
+        nbytes = int(_lib.lib().ggufmm_allreduce_buffer_bytes(n, self.world))
+        if nbytes == 0:
+            raise ValueError(f"no peer all-reduce for n={n} (a multiple of 4, at most {self.MAX_N} values)")
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        try:
+            symm_mem.enable_symm_mem_for_group(group.group_name)
+        except Exception:  # already enabled, or not needed by this torch
+            pass
+        self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group.group_name)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every buffer is zero before any GPU publishes into it
+        self.ptrs = (ctypes.c_void_p * self.world)(*self.handle.buffer_ptrs)
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
+        """out = the sum of every rank's x (+ residual), identical on every rank; x, out
+        and residual fp32, contiguous, n values; out may be x."""
+        if x.dtype != torch.float32 or not x.is_contiguous() or x.numel() != self.n:
+            raise ValueError(f"x must be a contiguous float32 tensor of {self.n} values")
+        out = x if out is None else out
+        dev = x.device
+        with torch.cuda.device(dev):
+            st = _lib.lib().ggufmm_allreduce(x.data_ptr(), out.data_ptr(), self.n, self.ptrs, self.world, self.rank,
+                                             residual.data_ptr() if residual is not None else None, _stream(dev))
+        _lib.check(st, "ggufmm_allreduce")
+        return out
+
+
+class PeerGather:
+    """Output buffers for the N-split GEMM whose epilogue all-gathers over NVLink
+    (``gemm_allgather``): on every GPU of the group one symmetric-memory buffer holding
+    the device barrier's flags and the full [m, n_total] output. Creating it is a
+    collective. ``y`` is this GPU's full output (valid after ``gemm_allgather``)."""
+
+    def __init__(self, m: int, n_total: int, dtype: torch.dtype = torch.bfloat16, group=None,
+                 device: torch.device | None = None):
+        import ctypes
+
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group or dist.group.WORLD
+        self.world, self.rank, self.m, self.n_total, self.dtype = (dist.get_world_size(group),
+                                                                   dist.get_rank(group), m, n_total, dtype)
+        es = torch.empty((), dtype=dtype).element_size()
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        try:
+            symm_mem.enable_symm_mem_for_group(group.group_name)
+        except Exception:  # already enabled, or not needed by this torch
+            pass
+        self.hdr = int(_lib.lib().ggufmm_allreduce_buffer_bytes(0, self.world))  # the barrier's flags
+        self.buf = symm_mem.empty(self.hdr + m * n_total * es, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, group.group_name)
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
+        self.ptrs = (ctypes.c_void_p * self.world)(*self.handle.buffer_ptrs)
+        self.y_ptrs = (ctypes.c_void_p * self.world)(*[p + self.hdr for p in self.handle.buffer_ptrs])
+        self.y = self.buf[self.hdr:].view(dtype).view(m, n_total)
+
+
+def gemm_allgather(x: torch.Tensor, w_local: GGUFQuantTensor, gather: PeerGather) -> torch.Tensor:
+    """x @ W^T for a weight split by output rows over the gather's GPUs: this rank's slice
+    ``w_local`` (n_total / world rows) is multiplied and every value is stored into every
+    GPU's output at its column (the all-gather in the GEMM's epilogue); a device-side
+    barrier then makes the full [M, n_total] output ``gather.y`` valid on every GPU."""
+    dev = _require_cuda(x, w_local.data)
+    x2 = _as_2d(x, w_local.k)
+    m = x2.shape[0]
+    if m != gather.m or w_local.n * gather.world != gather.n_total:
+        raise ValueError("activations / weight slice do not match the gather buffers")
+    ws = workspace_for(w_local, m)
+    with torch.cuda.device(dev):
+        lib = _lib.lib()
+        st = lib.ggufmm_gemm_allgather(w_local.data.data_ptr(), w_local.qtype, w_local.n, w_local.k, x2.data_ptr(),
+                                       _code(x2.dtype), m, x2.stride(0), gather.y_ptrs, gather.world,
+                                       gather.rank * w_local.n, _code(gather.dtype), gather.n_total, ws.data_ptr(),
+                                       ws.numel(), _stream(dev))
+        _lib.check(st, "ggufmm_gemm_allgather")
+        st = lib.ggufmm_peer_barrier(gather.ptrs, gather.world, gather.rank, _stream(dev))
+    _lib.check(st, "ggufmm_peer_barrier")
+    return gather.y
+
+
 def gemv_allreduce(x: torch.Tensor, w: GGUFQuantTensor, exchange: PeerExchange, out: torch.Tensor | None = None,
                    out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Decode GEMV summed over the exchange's GPUs in the same kernel (NVLink peer

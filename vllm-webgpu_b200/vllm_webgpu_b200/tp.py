@@ -147,6 +147,11 @@ class TensorParallelLayerLinears:
         self.matmul = matmul  # injectable (CPU tests); the GPU path uses the grouped kernels
         self.collective = True  # False leaves out the all-reduces (measuring what they cost)
         self._graphs: dict = {}
+        # the o / down all-reduces: the one-shot peer-memory kernel (ggufmm_allreduce) for
+        # decode-sized partials with GGUFMM_TP_ALLREDUCE=peer, NCCL by default
+        import os
+        self.peer_allreduce = matmul is None and os.environ.get("GGUFMM_TP_ALLREDUCE", "nccl") == "peer"
+        self._peer: dict = {}
         w = {}
         for p in ("q", "k", "v", "gate", "up"):
             n = weights[p].n
@@ -182,17 +187,28 @@ class TensorParallelLayerLinears:
             for w, o in zip(ws, outs):
                 ops.mul_mat(x, w, out=o)
 
+    def _allreduce(self, t: torch.Tensor) -> None:
+        if self.world == 1 or not self.collective:
+            return
+        if (self.peer_allreduce and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+                and t.numel() <= 1 << 16 and t.numel() % 4 == 0):
+            from . import ops
+            key = t.numel()
+            if key not in self._peer:
+                self._peer[key] = ops.PeerAllReduce(key, self.group, t.device)
+            self._peer[key](t)
+            return
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
     def forward(self, normed, attn_local, ffn_normed, act_local, bufs: dict) -> dict:
         """bufs: q, k, v, gate, up (this rank's output slices) and o, down (full
         width, fp32: the all-reduced sums)."""
         self._grouped(normed, ("q", "k", "v"), [bufs["q"], bufs["k"], bufs["v"]])
         self._mm(attn_local, self.w["o"], bufs["o"])
-        if self.world > 1 and self.collective:
-            dist.all_reduce(bufs["o"], op=dist.ReduceOp.SUM, group=self.group)
+        self._allreduce(bufs["o"])
         self._grouped(ffn_normed, ("gate", "up"), [bufs["gate"], bufs["up"]])
         self._mm(act_local, self.w["down"], bufs["down"])
-        if self.world > 1 and self.collective:
-            dist.all_reduce(bufs["down"], op=dist.ReduceOp.SUM, group=self.group)
+        self._allreduce(bufs["down"])
         return bufs
 
     __call__ = forward
