@@ -620,7 +620,7 @@ def run_ours(args, rank: int, world: int) -> None:
     if not args.no_batched:
         batched = {"workload": "q4k_llama3_8b_layer_decode", "path": "4 launch groups: ops.gemm_grouped (q/k/v, "
                    "gate/up) and ops.mul_mat (o, down); fused-dequant tcgen05 GEMM, K split where the "
-                   "weights have few 128-row tiles" + ("" if world == 1 else f"; tp{world} with 2 NCCL all-reduces")}
+                   "weights have few 128-row tiles" + ("" if world == 1 else f"; tp{world} with 2 all-reduces")}
         wbytes = sum(n * k // 256 * 144 for _, n, k in LAYER)
         for mb in (16, 64):
             xb = {nm: torch.randn((mb, kk), generator=g, device=dev).to(torch.bfloat16)
@@ -666,7 +666,9 @@ def run_ours(args, rank: int, world: int) -> None:
         del full
         wbytes = 3 * hid * inter // 256 * 144
         tpf = {"workload": "q4k_llama3_70b_ffn_tp", "tp": world, "weight_bytes_total": wbytes,
-               "path": "fused gate/up/SwiGLU GEMV (M<=8) or GEMMs, down projection, NCCL all-reduce; CUDA graph replay"}
+               "path": "fused gate/up/SwiGLU GEMV (M<=8) or GEMM with the SwiGLU epilogue, down projection, "
+                       "all-reduce (one-shot peer-memory kernel up to 65536 values, NCCL above); "
+                       "CUDA graph replay"}
         for mt in (1, 32, 2048):
             xt = torch.randn((mt, hid), generator=g, device=dev).to(torch.bfloat16)
             for _ in range(3):

@@ -24,6 +24,8 @@
 // returns. A peer that never publishes makes the wait give up after the bounded poll
 // count: the status word gets kErrWaitTimeout and out is not written. No multicast,
 // no NVLS: plain peer stores and local loads.
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace ggufmm {
@@ -122,11 +124,101 @@ __global__ void __launch_bounds__(kArThreads) allreduce_push_kernel(const ArArgs
   *reinterpret_cast<float4*>(a.out + i0) = s;
 }
 
+// ---- "LL" variant: each value travels with its generation in one 8-byte word ----
+// (gen << 32 | value bits), stored with 8-byte-element vector stores into slot
+// [gen & 1][rank] of every rank's buffer; a receiver polls its LOCAL words until all
+// carry the call's generation, so no fence and no separate flag are needed: one
+// NVLink write latency per call. The data region then holds 2 x world x n 8-byte words.
+__device__ __forceinline__ void st_v2u64(void* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_v2u64(const void* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__global__ void __launch_bounds__(kArThreads) allreduce_ll_kernel(const ArArgs a) {
+  __shared__ uint32_t s_gen;
+  __shared__ int s_ok;
+  const int c = blockIdx.x;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(a.buf[a.rank]);
+  uint32_t* my_gen = reinterpret_cast<uint32_t*>(mine + 8 * kArMaxCtas * 4) + c;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    s_gen = *reinterpret_cast<volatile uint32_t*>(my_gen) + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t gen = s_gen;
+  const uint64_t tag = static_cast<uint64_t>(gen) << 32;
+  const int64_t i0 = static_cast<int64_t>(c) * kArChunk + 4 * threadIdx.x;
+  const bool live = i0 < a.n;
+  const int64_t par_off = kArDataOff + static_cast<int64_t>(gen & 1u) * a.world * a.n * 8;
+  if (live) {
+    const float4 v = *reinterpret_cast<const float4*>(a.in + i0);
+    const uint64_t w0 = tag | __float_as_uint(v.x), w1 = tag | __float_as_uint(v.y);
+    const uint64_t w2 = tag | __float_as_uint(v.z), w3 = tag | __float_as_uint(v.w);
+    for (int p = 0; p < a.world; ++p) {
+      uint8_t* dst = reinterpret_cast<uint8_t*>(a.buf[p]) + par_off + (static_cast<int64_t>(a.rank) * a.n + i0) * 8;
+      st_v2u64(dst, w0, w1);
+      st_v2u64(dst + 16, w2, w3);
+    }
+  }
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool ok = true;
+  if (live) {
+    const uint32_t lim = g_wait_limit;
+    for (int q = 0; q < a.world && ok; ++q) {
+      const uint8_t* src = mine + par_off + (static_cast<int64_t>(q) * a.n + i0) * 8;
+      uint64_t w0, w1, w2, w3;
+      ok = false;
+      for (uint32_t it = 0; it < lim; ++it) {
+        ld_v2u64(src, w0, w1);
+        ld_v2u64(src + 16, w2, w3);
+        if (static_cast<uint32_t>(w0 >> 32) == gen && static_cast<uint32_t>(w1 >> 32) == gen &&
+            static_cast<uint32_t>(w2 >> 32) == gen && static_cast<uint32_t>(w3 >> 32) == gen) {
+          ok = true;
+          break;
+        }
+        if (it > 64) __nanosleep(32);
+      }
+      s.x += __uint_as_float(static_cast<uint32_t>(w0));
+      s.y += __uint_as_float(static_cast<uint32_t>(w1));
+      s.z += __uint_as_float(static_cast<uint32_t>(w2));
+      s.w += __uint_as_float(static_cast<uint32_t>(w3));
+    }
+  }
+  if (!ok) {
+    s_ok = 0;
+    atomicOr(&g_device_error, kErrWaitTimeout);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *my_gen = gen;
+  if (!s_ok || !live) return;
+  if (a.resid) {
+    const float4 r = *reinterpret_cast<const float4*>(a.resid + i0);
+    s.x += r.x;
+    s.y += r.y;
+    s.z += r.z;
+    s.w += r.w;
+  }
+  *reinterpret_cast<float4*>(a.out + i0) = s;
+}
+
+// GGUFMM_AR_PROTO=push selects the fenced push-and-flag kernel for data calls (the
+// barrier always uses it); the default is the LL kernel.
+bool ar_ll() {
+  static const bool on = [] {
+    const char* e = std::getenv("GGUFMM_AR_PROTO");
+    return !(e && e[0] == 'p');
+  }();
+  return on;
+}
+
 }  // namespace
 
 size_t allreduce_buffer_bytes(int64_t n, int world) {
   if (n < 0 || n > kArMaxN || n % 4 || world < 2 || world > 8) return 0;
-  return (kArDataOff + static_cast<size_t>(2) * world * n * 4 + 255) / 256 * 256;
+  return (kArDataOff + static_cast<size_t>(2) * world * n * 8 + 255) / 256 * 256;
 }
 
 cudaError_t launch_allreduce_oneshot(const float* in, float* out, int64_t n, void* const* bufs, int world, int rank,
@@ -150,6 +242,7 @@ cudaError_t launch_allreduce_oneshot(const float* in, float* out, int64_t n, voi
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (n > 0 && ar_ll()) return cudaLaunchKernelEx(&cfg, allreduce_ll_kernel, a);
   return cudaLaunchKernelEx(&cfg, allreduce_push_kernel, a);
 }
 

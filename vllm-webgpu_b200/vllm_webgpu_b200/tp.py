@@ -104,8 +104,23 @@ class TensorParallelSwiGLU:
             if add_here:
                 y.add_(residual)
         if self.world > 1:
-            dist.all_reduce(y, op=dist.ReduceOp.SUM, group=self.group)
+            self._allreduce(y)
         return y
+
+    def _allreduce(self, t: torch.Tensor) -> None:
+        """Sum over the ranks: the one-shot peer-memory kernel for decode-sized fp32
+        partials, NCCL otherwise (or with GGUFMM_TP_ALLREDUCE=nccl)."""
+        import os
+        if (self.fused_swiglu and t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+                and t.numel() <= 1 << 16 and t.numel() % 4 == 0
+                and os.environ.get("GGUFMM_TP_ALLREDUCE", "peer") != "nccl"):
+            from . import ops
+            peers = self.__dict__.setdefault("_peer", {})
+            if t.numel() not in peers:
+                peers[t.numel()] = ops.PeerAllReduce(t.numel(), self.group, t.device)
+            peers[t.numel()](t)
+            return
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def _down_allreduce(self, act: torch.Tensor):
         """Decode: the down projection and the all-reduce in one kernel over NVLink
@@ -148,9 +163,10 @@ class TensorParallelLayerLinears:
         self.collective = True  # False leaves out the all-reduces (measuring what they cost)
         self._graphs: dict = {}
         # the o / down all-reduces: the one-shot peer-memory kernel (ggufmm_allreduce) for
-        # decode-sized partials with GGUFMM_TP_ALLREDUCE=peer, NCCL by default
+        # decode-sized partials (3.9 us for 16 KB on 2 GPUs against 18.6 us for NCCL's, in
+        # a CUDA graph), NCCL above 65536 values or with GGUFMM_TP_ALLREDUCE=nccl
         import os
-        self.peer_allreduce = matmul is None and os.environ.get("GGUFMM_TP_ALLREDUCE", "nccl") == "peer"
+        self.peer_allreduce = matmul is None and os.environ.get("GGUFMM_TP_ALLREDUCE", "peer") != "nccl"
         self._peer: dict = {}
         w = {}
         for p in ("q", "k", "v", "gate", "up"):
