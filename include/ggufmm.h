@@ -214,20 +214,22 @@ int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t 
 
 /*
  * Decode GEMV whose result is all-reduced (summed) over `world` GPUs in the same
- * kernel, through NVLink peer memory: the tensor-parallel FFN's down projection
- * (each GPU holds a column slice of W over its share of the intermediate
- * dimension), replacing the GEMV followed by a separate NCCL all-reduce. Every
- * GPU of the group makes this call with the same shapes and `epoch`; each writes
- * its fp32 partial of every 16-row block into every GPU's exchange buffer over
- * NVLink, publishes a per-block flag (release, system scope), waits (bounded) for
- * the other GPUs' flags and stores the sum of the partials in rank order, so all
- * GPUs hold bit-identical y[m, n].
+ * kernel, through NVLink peer memory: the tensor-parallel FFN's / layer's down and o
+ * projections (each GPU holds a column slice of W over its share of the inner
+ * dimension), replacing the GEMV followed by a separate all-reduce. Every GPU of the
+ * group makes this call with the same shapes; each CTA's epilogue stores its fp32
+ * partials, each tagged with the call's generation in the same 8-byte word, into every
+ * GPU's exchange buffer over NVLink, then polls its own buffer (bounded) until the
+ * other GPUs' words of the same rows carry that generation and stores the sum of the
+ * partials in rank order, so all GPUs hold bit-identical y[m, n]. The generation is a
+ * per-CTA counter kept in the exchange buffer (device memory), so the call can be
+ * captured in a CUDA graph and replayed.
  *   peer_bufs  the `world` exchange buffers (device pointers valid on this GPU,
  *              e.g. from CUDA IPC / symmetric memory; 256-byte aligned), each
  *              ggufmm_gemv_allreduce_buffer_bytes(n, m_max, world) bytes and
  *              zero-filled before the first call
- *   epoch      1 for the first call on these buffers, +1 on every later call
- *              (partials alternate between two halves by epoch parity)
+ *   epoch      must be nonzero; not used otherwise (kept for compatibility: the
+ *              generation lives in device memory)
  * Q4_K / Q4_0, 1 <= M <= m_max <= 8, 2 <= world <= 8; otherwise as ggufmm_gemv.
  * A GPU whose peers never make the matching call gives up after a bounded wait
  * (ggufmm_device_status reports it). The reference has no multi-GPU path.

@@ -110,7 +110,8 @@ def test_swiglu_and_allreduce_host_validation(lib):
     assert ar(epoch=0) == L.ERR_ARG
     assert ar(b=(ctypes.c_void_p * 2)(P, P + 8)) == L.ERR_ALIGN
     # exchange buffer: 2 parities x world x m_max x n fp32, then 2 x world x row-block flags
-    assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 8, 2) == 2 * 2 * 8 * 8192 * 4 + 2 * 2 * (8192 // 16) * 4
+    # 4 KB of per-CTA generation counters + [2 parities][2 sources][8 tokens][8192] 8-byte tagged words
+    assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 8, 2) == 4096 + 2 * 2 * 8 * 8192 * 8
     assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 9, 2) == 0
     assert lib.ggufmm_gemv_allreduce_buffer_bytes(8192, 1, 1) == 0
 

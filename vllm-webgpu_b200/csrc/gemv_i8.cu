@@ -89,8 +89,9 @@ struct I8Args {
   const void* resid; // optional residual added to segment 0's y (y's dtype, row stride ldr; may alias y)
   int64_t ldr;
   // all-reduce over tp_world GPUs through peer memory (tp_world > 1): every GPU's
-  // exchange buffer, [2 parities][tp_world sources][m_max][n] fp32 partials then
-  // [2][tp_world][row blocks] u32 flags; y = the sum of the partials
+  // exchange buffer, [kTpHdr bytes: u32 generation per CTA][2 parities][tp_world
+  // sources][m_max][n] 8-byte words (generation << 32 | fp32 partial); y = the sum of
+  // the partials
   int tp_world, tp_rank;
   uint32_t epoch;
   int64_t m_max, tp_nrb, tp_flag_off;  // flag_off in bytes
@@ -133,24 +134,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   return false;
 }
 // ---- peer-memory (NVLink) exchange for the fused all-reduce ----
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// bounded: gives up (error word) rather than hang when a peer never publishes
-__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t want) {
-  const uint32_t lim = g_wait_limit;
-  for (uint32_t i = 0; i < lim; ++i) {
-    if (ld_acquire_sys(p) == want) return true;
-    if (i > 64) __nanosleep(128);
-  }
-  atomicOr(&g_device_error, kErrWaitTimeout);
-  return false;
-}
+constexpr int64_t kTpHdr = 4096;  // u32 generation per CTA (at most 1024 CTAs)
 
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -593,6 +585,7 @@ __global__ void __launch_bounds__((W + 2) * 32, MINB) gemv_i8_kernel(const I8Arg
       // ---------------- epilogue ----------------
       float gv[8];  // SwiGLU: this lane's gate sums of the current pair (one per token pass)
       float pv[8];  // all-reduce: this lane's partials of the current row block
+      uint32_t tp_gen = 0;  // all-reduce: this call's generation (this CTA's counter + 1)
 #pragma unroll
       for (int i = 0; i < 8; ++i) gv[i] = 0.f;
       for (int64_t blk = 0; blk < my_blocks; ++blk) {
@@ -655,9 +648,14 @@ __global__ void __launch_bounds__((W + 2) * 32, MINB) gemv_i8_kernel(const I8Arg
           for (int it = 0; it < a.m; ++it) out_pass(it);
         }
         if (EXT && a.tp_world > 1 && rank == 0) {
-          // this GPU's partials of the row block into every GPU's slot [par][tp_rank];
-          // published once per CTA after its last block (one system fence, one flag)
-          const uint32_t par = a.epoch & 1u;
+          // this GPU's partials of the row block into every GPU's slot [gen & 1][tp_rank],
+          // each value with the call's generation in the same 8-byte word (the receiver
+          // polls the words themselves: no fence, no flag)
+          if (blk == 0 && lane == 0)
+            tp_gen = *reinterpret_cast<volatile uint32_t*>(reinterpret_cast<uint32_t*>(a.peer[a.tp_rank]) + cid) + 1u;
+          tp_gen = __shfl_sync(0xFFFFFFFFu, tp_gen, 0);
+          const uint64_t tag = static_cast<uint64_t>(tp_gen) << 32;
+          const int64_t par = tp_gen & 1u;
           const int64_t nb = a.seg[0].n;
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
@@ -666,8 +664,10 @@ __global__ void __launch_bounds__((W + 2) * 32, MINB) gemv_i8_kernel(const I8Arg
             const int row = i & 15, half = (i >> 4) & 1, tok = i >> 5;
             const int64_t n_idx = r0 + phys_row(row, a.rg);
             if (half == 0 && n_idx < nb) {
-              const int64_t off = ((static_cast<int64_t>(par) * a.tp_world + a.tp_rank) * a.m_max + tok) * nb + n_idx;
-              for (int p = 0; p < a.tp_world; ++p) reinterpret_cast<float*>(a.peer[p])[off] = pv[it];
+              const int64_t off = ((par * a.tp_world + a.tp_rank) * a.m_max + tok) * nb + n_idx;
+              const uint64_t w = tag | __float_as_uint(pv[it]);
+              for (int p = 0; p < a.tp_world; ++p)
+                st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(a.peer[p] + kTpHdr) + off, w);
             }
           }
         }
@@ -683,38 +683,47 @@ __global__ void __launch_bounds__((W + 2) * 32, MINB) gemv_i8_kernel(const I8Arg
         if (lane == 0) mbar_arrive(&rempty[b]);
       }
       if (EXT && a.tp_world > 1 && rank == 0 && my_blocks > 0) {
-        // publish this CTA's partials (flag [par][tp_rank][cid] on every GPU), wait for
-        // the other GPUs' flags of the same CTA index (the same row blocks), then the
-        // sums in rank order -- the same bits on every GPU
-        const uint32_t par = a.epoch & 1u;
+        // the other GPUs' partials of the same row blocks (same CTA index: the row-block
+        // schedule is the same on every GPU) arrive as tagged words in this GPU's buffer:
+        // poll each until it carries this call's generation (bounded), then the sums in
+        // rank order -- the same bits on every GPU
+        const int64_t par = tp_gen & 1u;
         const int64_t nb = a.seg[0].n;
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        __syncwarp();
-        const int64_t fo = static_cast<int64_t>(par) * a.tp_world * a.tp_nrb + cid;
-        if (lane < a.tp_world)
-          st_release_sys(reinterpret_cast<uint32_t*>(a.peer[lane] + a.tp_flag_off) + fo + a.tp_rank * a.tp_nrb,
-                         a.epoch);
+        const uint64_t* mine = reinterpret_cast<const uint64_t*>(a.peer[a.tp_rank] + kTpHdr);
+        const uint32_t lim = g_wait_limit;
         bool ok2 = true;
-        if (lane < a.tp_world)
-          ok2 = wait_flag_sys(reinterpret_cast<const uint32_t*>(a.peer[a.tp_rank] + a.tp_flag_off) + fo +
-                                  lane * a.tp_nrb, a.epoch);
-        ok2 = __all_sync(0xFFFFFFFFu, ok2);
-        const float* mine = reinterpret_cast<const float*>(a.peer[a.tp_rank]);
         for (int64_t blk = 0; blk < my_blocks && ok2; ++blk) {
           int64_t r0;
           block_rows<EXT>(a, block_of<EXT>(a, cid, ncl, blk), r0);
-          for (int i = lane; i < kRows * a.m; i += 32) {
+          for (int i = lane; i < kRows * a.m && ok2; i += 32) {
             const int row = i & 15, tok = i >> 4;
             const int64_t n_idx = r0 + phys_row(row, a.rg);
             if (n_idx < nb) {
               float v = 0.f;
-              for (int p = 0; p < a.tp_world; ++p)
-                v += mine[((static_cast<int64_t>(par) * a.tp_world + p) * a.m_max + tok) * nb + n_idx];
+              for (int p = 0; p < a.tp_world && ok2; ++p) {
+                const uint64_t* src = mine + ((par * a.tp_world + p) * a.m_max + tok) * nb + n_idx;
+                uint64_t w = 0;
+                ok2 = false;
+                for (uint32_t q = 0; q < lim; ++q) {
+                  w = ld_relaxed_sys_u64(src);
+                  if (static_cast<uint32_t>(w >> 32) == tp_gen) {
+                    ok2 = true;
+                    break;
+                  }
+                  if (q > 64) __nanosleep(32);
+                }
+                v += __uint_as_float(static_cast<uint32_t>(w));
+              }
+              if (!ok2) break;
               if (a.resid) v += load_y_rt(a.resid, a.ytype, tok * a.ldr + n_idx);
               store_y_rt(a.seg[0].y, a.ytype, tok * a.seg[0].ldy + n_idx, v);
             }
           }
+          ok2 = __all_sync(0xFFFFFFFFu, ok2);
         }
+        if (!ok2 && lane == 0) atomicOr(&g_device_error, kErrWaitTimeout);
+        __syncwarp();
+        if (lane == 0) reinterpret_cast<uint32_t*>(a.peer[a.tp_rank])[cid] = tp_gen;  // this CTA's call done
       }
     } else {
       // ---------------- compute ----------------
@@ -996,12 +1005,8 @@ struct GemvTp {
   int64_t m_max;
   const void* const* bufs;
 };
-size_t gemv_tp_flag_offset(int64_t n, int64_t m_max, int world) {
-  return (static_cast<size_t>(2) * world * m_max * n * 4 + 255) / 256 * 256;
-}
 size_t gemv_tp_buffer_bytes(int64_t n, int64_t m_max, int world) {
-  const int64_t nrb = (n + kRows - 1) / kRows;
-  return gemv_tp_flag_offset(n, m_max, world) + (static_cast<size_t>(2) * world * nrb * 4 + 255) / 256 * 256;
+  return kTpHdr + (static_cast<size_t>(2) * world * m_max * n * 8 + 255) / 256 * 256;
 }
 
 cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -1043,7 +1048,7 @@ cudaError_t launch_gemv_i8_grouped(int nseg, const void* const* q, const int64_t
     a.epoch = tp->epoch;
     a.m_max = tp->m_max;
     a.tp_nrb = rb;
-    a.tp_flag_off = static_cast<int64_t>(gemv_tp_flag_offset(n[0], tp->m_max, tp->world));
+    a.tp_flag_off = 0;
     for (int i = 0; i < tp->world; ++i) a.peer[i] = reinterpret_cast<uint64_t>(tp->bufs[i]);
   }
   a.k = static_cast<int>(k);

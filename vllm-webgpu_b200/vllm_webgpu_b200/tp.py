@@ -167,6 +167,7 @@ class TensorParallelLayerLinears:
         # a CUDA graph), NCCL above 65536 values or with GGUFMM_TP_ALLREDUCE=nccl
         import os
         self.peer_allreduce = matmul is None and os.environ.get("GGUFMM_TP_ALLREDUCE", "peer") != "nccl"
+        self.fused_allreduce = matmul is None and os.environ.get("GGUFMM_TP_FUSED", "0") == "1"
         self._peer: dict = {}
         w = {}
         for p in ("q", "k", "v", "gate", "up"):
@@ -216,15 +217,30 @@ class TensorParallelLayerLinears:
             return
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
+    def _mm_allreduce(self, x, p: str, out) -> None:
+        """out = the all-reduced x W_p^T: in decode (M <= 8 on the integer GEMV) with
+        GGUFMM_TP_FUSED=1 one kernel that also all-reduces through NVLink peer memory
+        (ggufmm_gemv_allreduce), else the projection and a separate all-reduce."""
+        w = self.w[p]
+        if self.world > 1 and self.collective and self.fused_allreduce and x.is_cuda and out.dtype == torch.float32:
+            from . import ops
+            m = x.reshape(-1, x.shape[-1]).shape[0]
+            if m <= 8 and w.qtype in (2, 12) and ops.gemv_kernel(m, w, x.dtype) == ops.GEMV_INT8:
+                ex = self._peer.get(("x", p))
+                if ex is None:
+                    ex = self._peer[("x", p)] = ops.PeerExchange(w.n, 8, self.group, x.device)
+                ops.gemv_allreduce(x, w, ex, out=out)
+                return
+        self._mm(x, w, out)
+        self._allreduce(out)
+
     def forward(self, normed, attn_local, ffn_normed, act_local, bufs: dict) -> dict:
         """bufs: q, k, v, gate, up (this rank's output slices) and o, down (full
         width, fp32: the all-reduced sums)."""
         self._grouped(normed, ("q", "k", "v"), [bufs["q"], bufs["k"], bufs["v"]])
-        self._mm(attn_local, self.w["o"], bufs["o"])
-        self._allreduce(bufs["o"])
+        self._mm_allreduce(attn_local, "o", bufs["o"])
         self._grouped(ffn_normed, ("gate", "up"), [bufs["gate"], bufs["up"]])
-        self._mm(act_local, self.w["down"], bufs["down"])
-        self._allreduce(bufs["down"])
+        self._mm_allreduce(act_local, "down", bufs["down"])
         return bufs
 
     __call__ = forward
