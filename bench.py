@@ -379,7 +379,9 @@ def run_ours(args, rank: int, world: int) -> None:
         comm = {"step_us_without_allreduce": round(ms_nc / steps * 1e3, 2),
                 "allreduce_share_of_step": round(max(0.0, 1.0 - ms_nc / ms), 4),
                 "allreduces_per_step": 2, "allreduce_bytes": m * hid * 4,
-                "collective": ("ggufmm_allreduce (one-shot, NVLink peer memory, fp32)" if tp0.peer_allreduce
+                "collective": ("ggufmm_gemv_allreduce (the o / down GEMV and the all-reduce in one kernel, "
+                               "NVLink peer memory, fp32)" if tp0.fused_allreduce else
+                               "ggufmm_allreduce (one-shot, NVLink peer memory, fp32)" if tp0.peer_allreduce
                                else "NCCL all_reduce (fp32)")}
         del nb, ns
 

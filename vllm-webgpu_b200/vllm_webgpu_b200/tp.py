@@ -11,9 +11,12 @@ vllm_webgpu/v1/worker.py:56-59). This module is the B200 addition:
   superblocks);
 * each rank computes silu(x Wg_r^T) * (x Wu_r^T) and its partial
   y_r = a_r Wd_r^T with the sm_100a kernels, then ONE all-reduce (sum) of the
-  [M, hidden] partials joins the ranks: NCCL over NVLink / NVSwitch, or (opt-in,
+  [M, hidden] partials joins the ranks: the one-shot peer-memory all-reduce
+  (ops.PeerAllReduce) for decode-sized partials, NCCL above; or (opt-in,
   GGUFMM_TP_FUSED=1, decode M <= 8) one kernel that computes the down projection
   and exchanges the partials through NVLink peer memory (ops.gemv_allreduce).
+* TensorParallelLayerLinears splits all seven projections of a layer the same
+  way, with the o / down GEMV and its all-reduce in one kernel in decode.
 
 The matmul callable is injectable so the sharding and the collective can be
 tested on CPU ranks (gloo) against the oracle; on GPUs it is always
@@ -70,8 +73,8 @@ class TensorParallelSwiGLU:
         self.matmul = matmul
         self.reduce_dtype = reduce_dtype
         # decode down projection + all-reduce fused over NVLink peer memory: opt-in
-        # (GGUFMM_TP_FUSED=1); at 2 GPUs it measures 93 us per M=1 step of the 70B FFN
-        # against 82 us for the GEMV + NCCL all-reduce, so NCCL is the default
+        # (GGUFMM_TP_FUSED=1); at 2 GPUs it measures 73.7 us per M=1 step of the 70B FFN
+        # against 72.3 us for the GEMV + the one-shot peer all-reduce, the default
         import os
         self.fused_allreduce = self.fused_swiglu and reduce_dtype == torch.float32 and \
             os.environ.get("GGUFMM_TP_FUSED", "0") == "1"
@@ -167,7 +170,9 @@ class TensorParallelLayerLinears:
         # a CUDA graph), NCCL above 65536 values or with GGUFMM_TP_ALLREDUCE=nccl
         import os
         self.peer_allreduce = matmul is None and os.environ.get("GGUFMM_TP_ALLREDUCE", "peer") != "nccl"
-        self.fused_allreduce = matmul is None and os.environ.get("GGUFMM_TP_FUSED", "0") == "1"
+        # o / down GEMV and all-reduce in one kernel in decode (35.6 against 37.6 us per layer
+        # step on 2 GPUs); GGUFMM_TP_FUSED=0 runs the GEMV and ggufmm_allreduce separately
+        self.fused_allreduce = matmul is None and os.environ.get("GGUFMM_TP_FUSED", "1") != "0"
         self._peer: dict = {}
         w = {}
         for p in ("q", "k", "v", "gate", "up"):
@@ -218,9 +223,9 @@ class TensorParallelLayerLinears:
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def _mm_allreduce(self, x, p: str, out) -> None:
-        """out = the all-reduced x W_p^T: in decode (M <= 8 on the integer GEMV) with
-        GGUFMM_TP_FUSED=1 one kernel that also all-reduces through NVLink peer memory
-        (ggufmm_gemv_allreduce), else the projection and a separate all-reduce."""
+        """out = the all-reduced x W_p^T: in decode (M <= 8 on the integer GEMV) one kernel
+        that also all-reduces through NVLink peer memory (ggufmm_gemv_allreduce), else the
+        projection and a separate all-reduce."""
         w = self.w[p]
         if self.world > 1 and self.collective and self.fused_allreduce and x.is_cuda and out.dtype == torch.float32:
             from . import ops
