@@ -465,9 +465,18 @@ def run_ours(args, rank: int, world: int) -> None:
             tps[c].graph_step(d["normed"], d["attn_out"], d["ffn_normed"], d["ffn_act"], ebufs, stage_in=si,
                               stage_out=so)
 
+    done = torch.cuda.Event()
+
+    def host_wait() -> None:
+        # spin on an event recorded after the step (a blocking stream sync adds the
+        # thread's wake-up latency to every step)
+        done.record(stream)
+        while not done.query():
+            pass
+
     def e2e_step(c: int) -> None:
         run_graph(c, True)
-        stream.synchronize()
+        host_wait()
 
     for i in range(5):
         e2e_step(i % copies)
@@ -495,15 +504,15 @@ def run_ours(args, rank: int, world: int) -> None:
 
     def only_h2d():
         din.copy_(hin, non_blocking=True)
-        stream.synchronize()
+        host_wait()
 
     def only_graph():
         run_graph(0, False)
-        stream.synchronize()
+        host_wait()
 
     def only_d2h():
         hout.copy_(dout, non_blocking=True)
-        stream.synchronize()
+        host_wait()
     e2e_parts = {"h2d_and_wait_us": round(host_us(only_h2d), 2), "graph_replay_and_wait_us": round(host_us(only_graph), 2),
                  "d2h_and_wait_us": round(host_us(only_d2h), 2), "step_us": round(e2e_ms / e2e_steps * 1e3, 2),
                  "device_step_us": round(ms / steps * 1e3, 2)}
@@ -729,7 +738,7 @@ def run_ours(args, rank: int, world: int) -> None:
                     "d2h_bytes_per_step": d2h, "breakdown": e2e_parts,
                     "path": ("LlamaB200Model.layer_linears_graph" if world == 1 else "TensorParallelLayerLinears.graph_step")
                     + " (one CUDA-graph replay per step holding the packed H2D copy from pinned host memory, the "
-                      "projections and the packed D2H copy), and a host wait per step"},
+                      "projections and the packed D2H copy), and a host wait per step (spin on an event)"},
             "gpu_launches": len(GROUPS) * steps * repeats,
             "comm": comm,
             "clocks": clocks,

@@ -327,7 +327,7 @@ int ggufmm_gemv_kernel(int qtype, int64_t n, int64_t k, int64_t m, int x_dtype) 
   const int64_t row_bytes = k / block_of(qtype) * bytes_of(qtype);
   if (row_bytes % 16 == 0 && gemv_i8_supported(qtype, k, static_cast<int>(m))) return GGUFMM_GEMV_INT8;
   if (gemv_mma_supported(qtype, n, k, static_cast<int>(m), x_dtype)) return GGUFMM_GEMV_F16;
-  return row_bytes % 16 ? GGUFMM_ERR_ALIGN : GGUFMM_GEMV_STREAM;
+  return row_bytes % 16 ? static_cast<int>(GGUFMM_ERR_ALIGN) : static_cast<int>(GGUFMM_GEMV_STREAM);
 }
 
 int ggufmm_gemv_swiglu(const void* q_gate, const void* q_up, int qtype, int64_t n, int64_t k, const void* x,
