@@ -280,8 +280,11 @@ int ggufmm_allreduce(const float* in, float* out, int64_t n, void* const* peer_b
                      const float* resid, void* stream);
 
 /*
- * Bytes of workspace ggufmm_gemm needs for this problem (0 for unsupported
- * arguments). Size it once for the largest M and reuse it.
+ * Bytes of workspace ggufmm_gemm uses for this problem on the current device (0
+ * for unsupported arguments): the fp16 weight and activations (required; this
+ * part grows with M) followed by fp32 partial tiles for the GEMM's tail split
+ * (optional: when the workspace is shorter the last wave of tiles runs unsplit).
+ * Size it once for the largest M and reuse it.
  */
 size_t ggufmm_gemm_workspace_size(int qtype, int64_t m, int64_t n, int64_t k);
 

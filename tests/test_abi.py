@@ -38,6 +38,10 @@ def test_geometry(lib):
 
 def test_workspace_size(lib):
     assert lib.ggufmm_gemm_workspace_size(12, 512, 14336, 4096) == 14336 * 4096 * 2 + 512 * 4096 * 2
+    # M = 2048: 896 tiles of 256 tokens on 148 SMs leave 8 in the last wave, each cut
+    # in 8 K slices whose fp32 partial tiles (256 x 128) follow the fp16 operands
+    assert lib.ggufmm_gemm_workspace_size(12, 2048, 14336, 4096) == (14336 * 4096 * 2 + 2048 * 4096 * 2
+                                                                     + 8 * 8 * 256 * 128 * 4)
     assert lib.ggufmm_gemm_workspace_size(12, 1, 10, 100) == 0  # K not a block multiple
     assert lib.ggufmm_gemm_workspace_size(99, 1, 10, 256) == 0
 

@@ -28,6 +28,16 @@ def _swiglu_ref(x, rg, ru, qt, n, k):
     return g / (1.0 + np.exp(-g)) * u
 
 
+def _gemm_unsplit(x, w):
+    """ops.gemm with a workspace that holds only the fp16 operands: the persistent
+    GEMM then runs its last wave unsplit, as the epilogue path's GEMM does, so the
+    two accumulate in the same order."""
+    from vllm_webgpu_b200 import ops
+    m = x.shape[0]
+    ws = torch.empty(w.n * w.k * 2 + (m * w.k * 2 + 255) // 256 * 256, dtype=torch.uint8, device=x.device)
+    return ops.gemm(x, w, out_dtype=torch.float32, workspace=ws)
+
+
 def _check_swiglu(y, x, gate, up, rg, ru, qt, n, k):
     """Decode (M <= 8, the integer / fp16 GEMV): against the oracle SwiGLU at 1.5 x 2e-3.
     Above it the GEMM runs on fp16 operands, so each of gate and up is within 2e-3 of the
@@ -39,8 +49,8 @@ def _check_swiglu(y, x, gate, up, rg, ru, qt, n, k):
     if x.shape[0] <= ops.GEMV_MAX_M:
         assert O.rel_err(y.cpu().numpy(), _swiglu_ref(xn, rg, ru, qt, n, k)) <= 1.5 * TOL
         return
-    g = ops.gemm(x, gate, out_dtype=torch.float32)
-    u = ops.gemm(x, up, out_dtype=torch.float32)
+    g = _gemm_unsplit(x, gate)
+    u = _gemm_unsplit(x, up)
     assert O.rel_err(g.cpu().numpy(), O.matmul_ref(xn, rg, qt, n, k)) <= TOL
     assert O.rel_err(u.cpu().numpy(), O.matmul_ref(xn, ru, qt, n, k)) <= TOL
     ref = (torch.nn.functional.silu(g.double()) * u.double()).cpu().numpy()

@@ -51,6 +51,71 @@ def test_gemm_prefill_config(cuda, qt, m):
     assert _check(qt, m, 14336, 4096, rows=384) <= TOL
 
 
+def _tail_plan(tiles, nk, sms):
+    """K slices of the tiles left after the full waves (1: no split), and the tiles run whole."""
+    rest = tiles % sms
+    sl = min(sms // rest, nk // 8) if rest else 1
+    if sl < 2:
+        return 1, tiles
+    kper = -(-nk // sl)
+    sl = -(-nk // kper)
+    return (sl, tiles - rest) if sl >= 2 else (1, tiles)
+
+
+def _persistent_plan(n, m, k, sms=148):
+    """The persistent GEMM's token-tile width and tail split: min over widths of
+    waves x (width + 192), the split tail counted as 1/slices + 0.15 of a wave."""
+    nt, nk = (n + 127) // 128, (k + 63) // 64
+    best = None
+    for bn in (256, 224, 192, 160, 128):
+        tiles = ((m + bn - 1) // bn) * nt
+        sl, _ = _tail_plan(tiles, nk, sms)
+        waves = tiles // sms + 1 / sl + 0.15 if sl > 1 else -(-tiles // sms)
+        cost = waves * (bn + 192)
+        if best is None or cost < best[1] * 0.999:
+            best = (bn, cost, sl)
+    return best[0], best[2]
+
+
+@pytest.mark.parametrize("n,m,bn,slices", [
+    (14336, 1000, 256, 4),   # full waves + a tail of 4 tiles cut in 4 K slices
+    (20000, 194, 224, 4),    # ragged weight tiles, a tail of 9 tiles
+    (4096, 647, 192, 1),     # no split: the tiles fill whole waves
+    (4096, 300, 160, 2),     # less than one wave: every tile split
+    (1024, 300, 128, 4),
+    (14336, 301, 160, 1),
+])
+def test_gemm_persistent_widths_and_tail_split(cuda, n, m, bn, slices):
+    """Every token-tile width of the persistent GEMM (two accumulators at a
+    power-of-two TMEM stride, ragged last token tile) and its K-split tail
+    (fp32 partial tiles summed in order by the reduce pass); K = 2048."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _persistent_plan(n, m, 2048, sms) == (bn, slices)
+    assert _check(O.Q4_K, m, n, 2048, rows=256) <= TOL
+
+
+def test_gemm_tail_split_deterministic_and_matches_unsplit(cuda):
+    """The split tail sums its slices in a fixed order: identical bits on every
+    call, and within fp32 rounding of the same GEMM without the split (a
+    workspace too small for the partials)."""
+    from vllm_webgpu_b200 import _lib, ops
+    m, n, k = 1000, 14336, 2048
+    raw = O.make_weights(n, k, O.Q4_K, seed=3)
+    w = _wt(raw, O.Q4_K, n, k)
+    x = torch.from_numpy(O.make_activations(m, k, seed=4)).to(torch.bfloat16).cuda()
+    full = int(_lib.lib().ggufmm_gemm_workspace_size(O.Q4_K, m, n, k))
+    base = n * k * 2 + m * k * 2
+    assert full > base  # this shape splits its tail
+    y1 = ops.gemm(x, w, out_dtype=torch.float32)
+    y2 = ops.gemm(x, w, out_dtype=torch.float32)
+    ws = torch.empty(base, dtype=torch.uint8, device="cuda")
+    y0 = ops.gemm(x, w, out_dtype=torch.float32, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    rms = y0.float().pow(2).mean().sqrt()
+    assert float((y1 - y0).abs().max() / rms) < 1e-4
+
+
 @pytest.mark.parametrize("qt", [O.Q4_K, O.Q8_0], ids=lambda q: QNAMES[q])
 def test_gemm_many_tiles_per_cta_ragged(cuda, qt):
     """785 tiles (5 token tiles x 157 weight tiles, both ragged): several tiles per

@@ -50,7 +50,8 @@ cudaError_t launch_allreduce_oneshot(const float* in, float* out, int64_t n, voi
                                      const void* resid, cudaStream_t st);
 cudaError_t allreduce_device_error(int* v, int clear, cudaStream_t st);
 cudaError_t launch_gemm_f16_peers(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k,
-                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st);
+                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st,
+                                  float* part, size_t part_bytes);
 cudaError_t allreduce_set_wait_limit(uint32_t polls);
 cudaError_t gemm_set_wait_limit(uint32_t polls);
 cudaError_t gemv_mma_set_wait_limit(uint32_t polls);
@@ -69,7 +70,8 @@ struct GemvTp {
 };
 size_t gemv_tp_buffer_bytes(int64_t n, int64_t m_max, int world);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                            int64_t ldy, cudaStream_t st);
+                            int64_t ldy, cudaStream_t st, float* part, size_t part_bytes);
+size_t gemm_tail_bytes(int64_t n, int64_t m, int64_t k);
 
 struct DevInfo {
   int sms = 0;
@@ -411,17 +413,31 @@ static bool fused_gemm_enabled() {
   return on;
 }
 
+// Two-pass GEMM workspace: [fp16 weight][fp16 activations][fp32 partials of the
+// GEMM's tail split]. The first two are required; the GEMM splits its last wave
+// along K only when the workspace also holds the third.
+static size_t gemm_ws_required(int64_t m, int64_t n, int64_t k) {
+  return round256(static_cast<size_t>(n) * k * 2) + round256(static_cast<size_t>(m) * k * 2);
+}
 size_t ggufmm_gemm_workspace_size(int qtype, int64_t m, int64_t n, int64_t k) {
   if (!block_of(qtype) || m <= 0 || n <= 0 || k <= 0 || k % block_of(qtype)) return 0;
-  return round256(static_cast<size_t>(n) * k * 2) + round256(static_cast<size_t>(m) * k * 2);
+  return gemm_ws_required(m, n, k) + round256(gemm_tail_bytes(n, m, k));
+}
+// The tail-split region of a two-pass workspace (null when it does not fit).
+static float* gemm_tail_region(void* workspace, size_t workspace_bytes, int64_t m, int64_t n, int64_t k,
+                               size_t* bytes) {
+  const size_t req = gemm_ws_required(m, n, k), tail = gemm_tail_bytes(n, m, k);
+  *bytes = 0;
+  if (tail == 0 || workspace_bytes < req + tail) return nullptr;
+  *bytes = workspace_bytes - req;
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + req);
 }
 
 int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, int x_dtype, int64_t m, int64_t ldx,
                 void* y, int y_dtype, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
   int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy);
   if (s) return s;
-  const size_t need = ggufmm_gemm_workspace_size(qtype, m, n, k);
-  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < gemm_ws_required(m, n, k)) return GGUFMM_ERR_WORKSPACE;
   if (!aligned(q, 2) || !aligned(workspace, 256) || !aligned(y, elem_size(y_dtype)) ||
       !aligned(x, elem_size(x_dtype)))
     return GGUFMM_ERR_ALIGN;
@@ -444,7 +460,9 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   uint8_t* x16 = w16 + round256(static_cast<size_t>(n) * k * 2);
   cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
   if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
-  if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st);
+  size_t tail_bytes = 0;
+  float* tail = gemm_tail_region(workspace, workspace_bytes, m, n, k, &tail_bytes);
+  if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st, tail, tail_bytes);
   return cuda_status(e);
 }
 
@@ -461,8 +479,7 @@ int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qt
     nmax = std::max(nmax, n[i]);
     fused = fused && aligned(q[i], 16);
   }
-  const size_t need = ggufmm_gemm_workspace_size(qtype, m, nmax, k);
-  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < gemm_ws_required(m, nmax, k)) return GGUFMM_ERR_WORKSPACE;
   if (!aligned(workspace, 256) || !aligned(x, elem_size(x_dtype))) return GGUFMM_ERR_ALIGN;
   for (int i = 0; i < nseg; ++i)
     if (!aligned(q[i], 2) || !aligned(y[i], elem_size(y_dtype))) return GGUFMM_ERR_ALIGN;
@@ -528,7 +545,8 @@ static int gemm_ffn(int nseg, const void* const* qs, int qtype, int64_t n, int64
     for (int i = 0; i < nseg && e == cudaSuccess; ++i) {  // dequantize -> fp16, tcgen05 GEMM into fp32 columns
       e = launch_dequant(qs[i], qtype, n, k, w16, GGUFMM_F16, st);
       if (e == cudaSuccess)
-        e = launch_gemm_f16(w16, x16, n, m, k, reinterpret_cast<float*>(part) + i * n, GGUFMM_F32, ntot, st);
+        e = launch_gemm_f16(w16, x16, n, m, k, reinterpret_cast<float*>(part) + i * n, GGUFMM_F32, ntot, st, nullptr,
+                            0);
     }
   }
   if (e == cudaSuccess)
@@ -579,8 +597,7 @@ int ggufmm_gemm_allgather(const void* q, int qtype, int64_t n, int64_t k, const 
   int s = check_matmul_args(q, qtype, n, k, x, x_dtype, m, ldx, y_peers[0], y_dtype, ldy);
   if (s) return s;
   if (col0 < 0 || col0 + n > ldy) return GGUFMM_ERR_SHAPE;
-  const size_t need = ggufmm_gemm_workspace_size(qtype, m, n, k);
-  if (!workspace || workspace_bytes < need) return GGUFMM_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < gemm_ws_required(m, n, k)) return GGUFMM_ERR_WORKSPACE;
   if (!aligned(q, 2) || !aligned(workspace, 256) || !aligned(x, elem_size(x_dtype))) return GGUFMM_ERR_ALIGN;
   for (int i = 0; i < world; ++i)
     if (!y_peers[i] || !aligned(y_peers[i], elem_size(y_dtype))) return GGUFMM_ERR_ALIGN;
@@ -591,7 +608,10 @@ int ggufmm_gemm_allgather(const void* q, int qtype, int64_t n, int64_t k, const 
   uint8_t* x16 = w16 + round256(static_cast<size_t>(n) * k * 2);
   cudaError_t e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
   if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
-  if (e == cudaSuccess) e = launch_gemm_f16_peers(w16, x16, n, m, k, y_peers, world, col0, y_dtype, ldy, st);
+  size_t tail_bytes = 0;
+  float* tail = gemm_tail_region(workspace, workspace_bytes, m, n, k, &tail_bytes);
+  if (e == cudaSuccess)
+    e = launch_gemm_f16_peers(w16, x16, n, m, k, y_peers, world, col0, y_dtype, ldy, st, tail, tail_bytes);
   return cuda_status(e);
 }
 
@@ -606,7 +626,7 @@ int ggufmm_mul_mat(const void* q, int qtype, int64_t n, int64_t k, const void* x
   // Q4_K shapes that only the streaming GEMV fits run faster on the fused-dequant GEMM,
   // when the caller passed a workspace for it
   const bool gemm_better = qtype == kQ4_K && workspace &&
-                           workspace_bytes >= ggufmm_gemm_workspace_size(qtype, m, n, k) &&
+                           workspace_bytes >= gemm_ws_required(m, n, k) &&
                            ggufmm_gemv_kernel(qtype, n, k, m, x_dtype) == GGUFMM_GEMV_STREAM;
   if (gemv_ok && !gemm_better)
     return ggufmm_gemv(q, qtype, n, k, x, x_dtype, m, ldx, y, y_dtype, ldy, stream);

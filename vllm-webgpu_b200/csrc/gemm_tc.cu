@@ -50,6 +50,25 @@ __device__ __forceinline__ void store_out(void* y, const PeerOut& po, int ytype,
   for (int p = 0; p < po.world; ++p) store_y_rt(reinterpret_cast<void*>(po.y[p]), ytype, mm * ldy + po.col0 + nrow, v);
 }
 
+// tcgen05.alloc takes a power of two >= 32 columns.
+__host__ __device__ constexpr uint32_t tmem_cols_pow2(uint32_t c) {
+  uint32_t p = 32;
+  while (p < c) p <<= 1;
+  return p;
+}
+
+// Tail split of the persistent GEMM. The first `whole` tiles run whole, as the
+// CTAs' first full waves; each of the remaining tiles is cut along K into
+// `slices` pieces of `kper` k-blocks, one piece per CTA, so the last wave lasts
+// 1/slices of a tile instead of a whole one. A piece leaves its fp32 partial tile
+// in part[piece][column][row] and gemm_tail_reduce_kernel adds the slices in order.
+struct TailSplit {
+  float* part;
+  int whole;
+  int slices;  // 1: no split
+  int kper;
+};
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t kABytes = kTileW * kBK * 2;  // 16 KB
@@ -62,8 +81,8 @@ struct GemmSmem {
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-                   void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k,
-                              const PeerOut po) {
+                   void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k, const PeerOut po,
+                   const TailSplit) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles need 1024-byte aligned bases
@@ -173,7 +192,7 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                               void* __restrict__ y, int ytype, int64_t ldy, int n, int m, int k,
-                              const PeerOut po) {
+                              const PeerOut po, const TailSplit ts) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -183,11 +202,34 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
+  // the two accumulators start half the (power-of-two) allocation apart
+  constexpr uint32_t kAccStride = tmem_cols_pow2(2 * BN) / 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mtiles = (m + BN - 1) / BN, ntiles = (n + kTileW - 1) / kTileW;
   const int tiles = mtiles * ntiles;
   const int nk = (k + kBK - 1) / kBK;
-  const int my_tiles = tiles > static_cast<int>(blockIdx.x) ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int bid = static_cast<int>(blockIdx.x), grid = static_cast<int>(gridDim.x);
+  // work items of this CTA: whole tiles bid, bid + grid, ... below ts.whole, then
+  // (tail split) piece bid of the remaining tiles
+  const int whole = ts.slices > 1 ? ts.whole : tiles;
+  const int my_whole = whole > bid ? (whole - 1 - bid) / grid + 1 : 0;
+  const bool has_piece = ts.slices > 1 && bid < (tiles - whole) * ts.slices;
+  const int my_tiles = my_whole + (has_piece ? 1 : 0);
+  // item i -> token / weight tile origin, k-block range, piece index (-1: whole tile)
+  auto item = [&](int i, int& m0, int& n0, int& kb0, int& kb1) -> int {
+    int t = bid + i * grid, piece = -1;
+    kb0 = 0;
+    kb1 = nk;
+    if (i >= my_whole) {
+      piece = bid;
+      t = whole + bid / ts.slices;
+      kb0 = (bid % ts.slices) * ts.kper;
+      kb1 = min(nk, kb0 + ts.kper);
+    }
+    m0 = (t % mtiles) * BN;
+    n0 = (t / mtiles) * kTileW;
+    return piece;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -204,7 +246,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * BN)
+                 "r"(tmem_cols_pow2(2 * BN))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -218,9 +260,9 @@ __global__ void __launch_bounds__(192, 1)
       int q = 0;  // running k-block index over all of this CTA's tiles
       bool ok = true;
       for (int i = 0; i < my_tiles && ok; ++i) {
-        const int t = blockIdx.x + i * gridDim.x;
-        const int m0 = (t % mtiles) * BN, n0 = (t / mtiles) * kTileW;
-        for (int kb = 0; kb < nk; ++kb, ++q) {
+        int m0, n0, kb0, kb1;
+        item(i, m0, n0, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int s = q % STAGES;
           if (!mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1)) {
             ok = false;
@@ -243,8 +285,10 @@ __global__ void __launch_bounds__(192, 1)
         const int b = i & 1;
         if (i >= 2 && !mbar_wait(&tempty[b], static_cast<uint32_t>(((i >> 1) - 1) & 1))) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc = tmem_d + static_cast<uint32_t>(b * BN);
-        for (int kb = 0; kb < nk; ++kb, ++q) {
+        const uint32_t acc = tmem_d + static_cast<uint32_t>(b) * kAccStride;
+        int m0, n0, kb0, kb1;
+        item(i, m0, n0, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++q) {
           const int s = q % STAGES;
           if (!mbar_wait(&full[s], (q / STAGES) & 1)) {
             ok = false;
@@ -256,7 +300,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t adesc = umma_smem_desc(a_addr), bdesc = umma_smem_desc(b_addr);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&tfull[b]);  // this tile's MMAs complete -> accumulator b ready
@@ -267,21 +311,33 @@ __global__ void __launch_bounds__(192, 1)
     const int quad = warp & 3;
     for (int i = 0; i < my_tiles; ++i) {
       const int b = i & 1;
-      const int t = blockIdx.x + i * gridDim.x;
-      const int m0 = (t % mtiles) * BN, n0 = (t / mtiles) * kTileW;
+      int m0, n0, kb0, kb1;
+      const int piece = item(i, m0, n0, kb0, kb1);
       if (!mbar_wait(&tfull[b], static_cast<uint32_t>((i >> 1) & 1))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int nrow = n0 + quad * 32 + lane;
-      const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(b * BN);
+      const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(b) * kAccStride;
+      if (piece >= 0) {
+        // partial tile, column-major: a warp's 32 rows are one 128-byte store
+        float* pp = ts.part + static_cast<int64_t>(piece) * BN * kTileW + quad * 32 + lane;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c0, r);
-        if (nrow < n) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int mm = m0 + c0 + j;
-            if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
+          for (int j = 0; j < 16; ++j) pp[(c0 + j) * kTileW] = __uint_as_float(r[j]);
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
+          if (nrow < n) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int mm = m0 + c0 + j;
+              if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
+            }
           }
         }
       }
@@ -294,7 +350,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(2 * BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(tmem_cols_pow2(2 * BN)) : "memory");
   }
 }
 
@@ -302,9 +358,62 @@ __global__ void __launch_bounds__(192, 1)
 static std::mutex g_gemm_attr_mu;
 static std::set<std::pair<const void*, int>> g_gemm_attr_done;
 
+static int device_sms() {
+  static const int sms = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      v = 148;
+    return v;
+  }();
+  return sms;
+}
+
+constexpr int kTailMinKb = 8;  // k-blocks per piece at least (pipeline fill amortised)
+
+// Tail split for `tiles` tiles of width bn on `sms` CTAs (slices 1: none). With
+// part_bytes < 0 the workspace is not limiting.
+static TailSplit tail_plan(int64_t tiles, int nk, int sms, int bn, int64_t part_bytes) {
+  TailSplit ts{nullptr, static_cast<int>(tiles), 1, nk};
+  const int64_t rest = tiles % sms;
+  if (rest == 0) return ts;
+  int64_t sl = std::min<int64_t>(sms / rest, nk / kTailMinKb);
+  const int64_t piece_bytes = static_cast<int64_t>(bn) * kTileW * 4;
+  if (part_bytes >= 0) sl = std::min<int64_t>(sl, part_bytes / (rest * piece_bytes));
+  if (sl < 2) return ts;
+  ts.kper = (nk + static_cast<int>(sl) - 1) / static_cast<int>(sl);
+  ts.slices = (nk + ts.kper - 1) / ts.kper;  // every piece non-empty
+  if (ts.slices < 2) return TailSplit{nullptr, static_cast<int>(tiles), 1, nk};
+  ts.whole = static_cast<int>(tiles - rest);
+  return ts;
+}
+
+// y[m0 + c, n0 + r] = sum over s (in order) of part[(t * slices + s) * bn + c][r] for
+// the split tiles t (the tail of the persistent GEMM).
+__global__ void __launch_bounds__(256) gemm_tail_reduce_kernel(const float* __restrict__ part, int whole, int rtiles,
+                                                               int slices, int bn, int mtiles, int n, int m,
+                                                               void* __restrict__ y, int ytype, int64_t ldy,
+                                                               const PeerOut po) {
+  const int64_t per_tile = static_cast<int64_t>(bn) * kTileW;
+  const int64_t total = rtiles * per_tile;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(i / per_tile);
+    const int64_t e = i - j * per_tile;
+    const int c = static_cast<int>(e / kTileW), r = static_cast<int>(e % kTileW);
+    const int t = whole + j;
+    const int mm = (t % mtiles) * bn + c, nrow = (t / mtiles) * kTileW + r;
+    if (mm >= m || nrow >= n) continue;
+    const float* pp = part + static_cast<int64_t>(j) * slices * per_tile + e;
+    float v = 0.f;
+    for (int s = 0; s < slices; ++s) v += pp[s * per_tile];
+    store_out(y, po, ytype, mm, ldy, nrow, v);
+  }
+}
+
 template <int BN, int STAGES, bool PERSIST = false>
 static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                  int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po = PeerOut{}) {
+                                  int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po, float* part,
+                                  size_t part_bytes) {
   using L = GemmSmem<BN, STAGES>;
   CUtensorMap mw, mx;
   if (!make_map_f16(&mw, w16, n, k, kTileW) || !make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
@@ -320,51 +429,120 @@ static cudaError_t launch_gemm_bn(const void* w16, const void* x16, int64_t n, i
       g_gemm_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
     }
   }
-  dim3 grid(static_cast<unsigned>((m + BN - 1) / BN), static_cast<unsigned>((n + kTileW - 1) / kTileW));
+  const int64_t mtiles = (m + BN - 1) / BN, tiles = mtiles * ((n + kTileW - 1) / kTileW);
+  const int nk = static_cast<int>((k + kBK - 1) / kBK);
+  dim3 grid(static_cast<unsigned>(mtiles), static_cast<unsigned>((n + kTileW - 1) / kTileW));
+  TailSplit ts{nullptr, static_cast<int>(tiles), 1, nk};
   if (PERSIST) {
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    grid = dim3(static_cast<unsigned>(std::min<int64_t>(static_cast<int64_t>(grid.x) * grid.y, sms)));
+    const int sms = device_sms();
+    if (part) ts = tail_plan(tiles, nk, sms, BN, static_cast<int64_t>(part_bytes));
+    ts.part = part;
+    grid = dim3(static_cast<unsigned>(ts.slices > 1 ? sms : std::min<int64_t>(tiles, sms)));
   }
   fn<<<grid, 192, L::kTotal, st>>>(mw, mx, y, ytype, ldy, static_cast<int>(n), static_cast<int>(m),
-                                   static_cast<int>(k), po);
+                                   static_cast<int>(k), po, ts);
+  e = cudaGetLastError();
+  if (e != cudaSuccess || ts.slices < 2) return e;
+  const int rtiles = static_cast<int>(tiles) - ts.whole;
+  const int64_t total = static_cast<int64_t>(rtiles) * BN * kTileW;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4 * 148));
+  gemm_tail_reduce_kernel<<<blocks, 256, 0, st>>>(part, ts.whole, rtiles, ts.slices, BN, static_cast<int>(mtiles),
+                                                  static_cast<int>(n), static_cast<int>(m), y, ytype, ldy, po);
   return cudaGetLastError();
 }
 
 cudaError_t gemm_device_error(int* v, int clear, cudaStream_t st) { return tu_device_error(v, clear, st); }
 cudaError_t gemm_set_wait_limit(uint32_t polls) { return tu_set_wait_limit(polls); }
 
+// Token-tile width of the persistent GEMM. Every CTA runs whole tiles, so the
+// last wave of ceil(tiles / SMs) is partly idle unless the tail is split along K
+// (tail_plan, when the caller gives partial-sum space). The width minimises
+// waves x (width + 192), with the tail counted as 1/slices + 0.15 of a wave; the 192
+// stands for a tile's fixed cost (accumulator hand-off, pipeline fill, and a
+// narrower tile's extra weight-tile fetches per flop). Without the split the
+// constant was fitted on B200 over K = 4096, N = 1792..14336, M = 512..8192
+// (Q4_K and Q6_K): the pick was the fastest width in every case, e.g. N = 3584,
+// M = 512 runs 128-wide in 49.9 us against 59.1 us 256-wide, while N = 14336,
+// M = 2048 stays 256-wide (253 us; 160-wide 266.8 us).
+// GGUFMM_GEMM_BN = 128|160|192|224|256 forces a width.
+static int persistent_bn(int64_t n, int64_t m, int64_t k, bool split) {
+  static const int forced = [] {
+    const char* e = std::getenv("GGUFMM_GEMM_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 160 || forced == 192 || forced == 224 || forced == 256) return forced;
+  const int sms = device_sms();
+  const int64_t ntiles = (n + kTileW - 1) / kTileW;
+  const int nk = static_cast<int>((k + kBK - 1) / kBK);
+  int best = 256;
+  double best_cost = -1;
+  for (int bn : {256, 224, 192, 160, 128}) {
+    const int64_t tiles = ((m + bn - 1) / bn) * ntiles;
+    const TailSplit ts = split ? tail_plan(tiles, nk, sms, bn, -1) : TailSplit{nullptr, 0, 1, nk};
+    // a split tail also pays its partial-tile stores and the reduce pass (~0.15 wave)
+    const double waves = ts.slices > 1 ? static_cast<double>(tiles / sms) + 1.0 / ts.slices + 0.15
+                                       : static_cast<double>((tiles + sms - 1) / sms);
+    const double cost = waves * (bn + 192);
+    if (best_cost < 0 || cost < best_cost * 0.999) best = bn, best_cost = cost;
+  }
+  return best;
+}
+
+// Bytes of fp32 partial sums the persistent GEMM's tail split uses for this shape
+// on the current device (0: no split).
+size_t gemm_tail_bytes(int64_t n, int64_t m, int64_t k) {
+  if (m <= 128) return 0;
+  const int bn = persistent_bn(n, m, k, true);
+  const int64_t tiles = ((m + bn - 1) / bn) * ((n + kTileW - 1) / kTileW);
+  const TailSplit ts = tail_plan(tiles, static_cast<int>((k + kBK - 1) / kBK), device_sms(), bn, -1);
+  if (ts.slices < 2) return 0;
+  return static_cast<size_t>(tiles - ts.whole) * ts.slices * bn * kTileW * 4;
+}
+
 // Tensor-core GEMM on fp16 operands already in device memory:
 // w16 [n, k], x16 [m, k] (both row-major, 16-byte aligned, k % 8 == 0).
 static cudaError_t launch_gemm_f16_po(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y,
-                                      int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po) {
-  if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po);
-  if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po);
-  if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+                                      int ytype, int64_t ldy, cudaStream_t st, const PeerOut& po, float* part,
+                                      size_t part_bytes) {
+  if (m <= 32) return launch_gemm_bn<32, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po, nullptr, 0);
+  if (m <= 64) return launch_gemm_bn<64, 8>(w16, x16, n, m, k, y, ytype, ldy, st, po, nullptr, 0);
+  if (m <= 128) return launch_gemm_bn<128, 6>(w16, x16, n, m, k, y, ytype, ldy, st, po, nullptr, 0);
   static const bool persist = [] {
     const char* e = std::getenv("GGUFMM_GEMM_PERSIST");
     return !(e && e[0] == '0');
   }();
-  if (persist) return launch_gemm_bn<256, 4, true>(w16, x16, n, m, k, y, ytype, ldy, st, po);
-  return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st, po);
+  if (!persist) return launch_gemm_bn<256, 4>(w16, x16, n, m, k, y, ytype, ldy, st, po, nullptr, 0);
+  static const bool split = [] {
+    const char* e = std::getenv("GGUFMM_GEMM_TAIL");
+    return !(e && e[0] == '0');
+  }();
+  if (!split) part = nullptr;
+  switch (persistent_bn(n, m, k, part != nullptr)) {
+    case 224: return launch_gemm_bn<224, 5, true>(w16, x16, n, m, k, y, ytype, ldy, st, po, part, part_bytes);
+    case 192: return launch_gemm_bn<192, 5, true>(w16, x16, n, m, k, y, ytype, ldy, st, po, part, part_bytes);
+    case 160: return launch_gemm_bn<160, 6, true>(w16, x16, n, m, k, y, ytype, ldy, st, po, part, part_bytes);
+    case 128: return launch_gemm_bn<128, 6, true>(w16, x16, n, m, k, y, ytype, ldy, st, po, part, part_bytes);
+    default: return launch_gemm_bn<256, 4, true>(w16, x16, n, m, k, y, ytype, ldy, st, po, part, part_bytes);
+  }
 }
 
+// part (fp32, part_bytes long; may be null): partial sums for the tail split.
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                            int64_t ldy, cudaStream_t st) {
-  return launch_gemm_f16_po(w16, x16, n, m, k, y, ytype, ldy, st, PeerOut{});
+                            int64_t ldy, cudaStream_t st, float* part, size_t part_bytes) {
+  return launch_gemm_f16_po(w16, x16, n, m, k, y, ytype, ldy, st, PeerOut{}, part, part_bytes);
 }
 
 // The same GEMM storing every output value into `world` outputs (all GPUs' [m, ldy]
 // buffers, peers' mapped over NVLink) at column col0 + row.
 cudaError_t launch_gemm_f16_peers(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k,
-                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st) {
+                                  void* const* ys, int world, int64_t col0, int ytype, int64_t ldy, cudaStream_t st,
+                                  float* part, size_t part_bytes) {
   if (world < 1 || world > 8) return cudaErrorInvalidValue;
   PeerOut po{};
   for (int i = 0; i < world; ++i) po.y[i] = reinterpret_cast<uint64_t>(ys[i]);
   po.world = world;
   po.col0 = col0;
-  return launch_gemm_f16_po(w16, x16, n, m, k, ys[0], ytype, ldy, st, po);
+  return launch_gemm_f16_po(w16, x16, n, m, k, ys[0], ytype, ldy, st, po, part, part_bytes);
 }
 
 }  // namespace ggufmm

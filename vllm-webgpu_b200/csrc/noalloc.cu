@@ -36,7 +36,7 @@ cudaError_t launch_dequant(const void* q, int qtype, int64_t n_rows, int64_t k, 
 cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, int64_t ldx, void* out,
                               cudaStream_t st);
 cudaError_t launch_gemm_f16(const void* w16, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,
-                            int64_t ldy, cudaStream_t st);
+                            int64_t ldy, cudaStream_t st, float* part, size_t part_bytes);
 int record_cuda_status(cudaError_t e);  // capi.cu: keeps the code for ggufmm_last_cuda_error
 
 // The library-owned scratch. In host code this name is only a stand-in for the
@@ -104,6 +104,6 @@ extern "C" int ggufmm_gemm_noalloc(const void* q, int qtype, int64_t n, int64_t 
   uint8_t* x16 = w16 + w_bytes;
   e = launch_dequant(q, qtype, n, k, w16, GGUFMM_F16, st);
   if (e == cudaSuccess) e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
-  if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st);
+  if (e == cudaSuccess) e = launch_gemm_f16(w16, x16, n, m, k, y, y_dtype, ldy, st, nullptr, 0);
   return record_cuda_status(e);
 }
