@@ -189,21 +189,31 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
       const int64_t ldy = sg.ldy[seg];
       const int64_t ntot = sg.row0[sg.nseg], grow = sg.row0[seg] + nrow;
       const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
+      // columns per TMEM wait (16 with 16 dequantizer warps: their register budget)
+      constexpr int kEpiChunk = DQ == 16 ? 16 : 32;
+      if (part) {
+        // a warp's 32 rows are one 128-byte store
+        float* pz = part + static_cast<int64_t>(blockIdx.z) * m * ntot + grow;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c0, r);
-        if (nrow < n) {
+        for (int c0 = 0; c0 < BN; c0 += kEpiChunk) {
+          uint32_t r[kEpiChunk];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int mm = m0 + c0 + j;
-            if (mm >= m) continue;
-            if (part)
-              part[(static_cast<int64_t>(blockIdx.z) * m + mm) * ntot + grow] = __uint_as_float(r[j]);
-            else
-              store_y_rt(y, ytype, static_cast<int64_t>(mm) * ldy + nrow, __uint_as_float(r[j]));
+          for (int h = 0; h < kEpiChunk; h += 16) tmem_ld16_async(tbase + c0 + h, r + h);
+          tmem_wait_ld();
+          if (nrow < n) {
+#pragma unroll
+            for (int j = 0; j < kEpiChunk; ++j) {
+              const int mm = m0 + c0 + j;
+              if (mm < m) pz[static_cast<int64_t>(mm) * ntot] = __uint_as_float(r[j]);
+            }
           }
         }
+      } else if (ytype == GGUFMM_BF16) {
+        drain_tile<BN, GGUFMM_BF16, kEpiChunk>(tbase, y, ldy, m0, m, nrow, n);
+      } else if (ytype == GGUFMM_F32) {
+        drain_tile<BN, GGUFMM_F32, kEpiChunk>(tbase, y, ldy, m0, m, nrow, n);
+      } else {
+        drain_tile<BN, GGUFMM_F16, kEpiChunk>(tbase, y, ldy, m0, m, nrow, n);
       }
     }
   } else {

@@ -50,32 +50,6 @@ __device__ __forceinline__ void store_out(void* y, const PeerOut& po, int ytype,
   for (int p = 0; p < po.world; ++p) store_y_rt(reinterpret_cast<void*>(po.y[p]), ytype, mm * ldy + po.col0 + nrow, v);
 }
 
-// One epilogue warp's 32 accumulator lanes (weight row nrow) x BN columns (tokens
-// m0..) into y[token, nrow] of type YT: 32 columns per TMEM wait, typed stores.
-template <int BN, int YT>
-__device__ __forceinline__ void drain_tile(uint32_t tbase, void* y, int64_t ldy, int m0, int m, int nrow, int n) {
-  const bool row_ok = nrow < n;
-  const int cols = min(BN, m - m0);  // live token columns of this tile
-#pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    uint32_t r[32];
-    tmem_ld16_async(tbase + c0, r);
-    tmem_ld16_async(tbase + c0 + 16, r + 16);
-    tmem_wait_ld();
-    if (row_ok) {
-      const int64_t base = static_cast<int64_t>(m0 + c0) * ldy + nrow;
-      if (c0 + 32 <= cols) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) store_y<YT>(y, base + j * ldy, __uint_as_float(r[j]));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < cols) store_y<YT>(y, base + j * ldy, __uint_as_float(r[j]));
-      }
-    }
-  }
-}
-
 // tcgen05.alloc takes a power of two >= 32 columns.
 __host__ __device__ constexpr uint32_t tmem_cols_pow2(uint32_t c) {
   uint32_t p = 32;
@@ -186,15 +160,23 @@ __global__ void __launch_bounds__(192, 1)
     if (ok) {
       const int nrow = n0 + quad * 32 + lane;
       const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
+      if (po.world == 0 && ytype == GGUFMM_BF16) {
+        drain_tile<BN, GGUFMM_BF16>(tbase, y, ldy, m0, m, nrow, n);
+      } else if (po.world == 0 && ytype == GGUFMM_F32) {
+        drain_tile<BN, GGUFMM_F32>(tbase, y, ldy, m0, m, nrow, n);
+      } else if (po.world == 0) {
+        drain_tile<BN, GGUFMM_F16>(tbase, y, ldy, m0, m, nrow, n);
+      } else {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c0, r);
-        if (nrow < n) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
+          if (nrow < n) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int mm = m0 + c0 + j;
-            if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
+            for (int j = 0; j < 16; ++j) {
+              const int mm = m0 + c0 + j;
+              if (mm < m) store_out(y, po, ytype, mm, ldy, nrow, __uint_as_float(r[j]));
+            }
           }
         }
       }

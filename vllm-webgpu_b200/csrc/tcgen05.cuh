@@ -71,6 +71,36 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// One epilogue warp's 32 accumulator lanes (weight row nrow) x BN columns (tokens
+// m0..) into y[token, nrow] of type YT: CH columns per TMEM wait (the loads'
+// latency is paid once per chunk), typed stores.
+// BN: columns this warp drains (a multiple of 16); CHMAX caps the chunk (registers).
+template <int BN, int YT, int CHMAX = 64>
+__device__ __forceinline__ void drain_tile(uint32_t tbase, void* y, int64_t ldy, int m0, int m, int nrow, int n) {
+  constexpr int CH = BN % 64 == 0 && CHMAX >= 64 ? 64 : BN % 32 == 0 && CHMAX >= 32 ? 32 : 16;
+  const bool row_ok = nrow < n;
+  const int cols = min(BN, m - m0);  // live token columns of this tile
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += CH) {
+    uint32_t r[CH];
+#pragma unroll
+    for (int h = 0; h < CH; h += 16) tmem_ld16_async(tbase + c0 + h, r + h);
+    tmem_wait_ld();
+    if (row_ok) {
+      const int64_t base = static_cast<int64_t>(m0 + c0) * ldy + nrow;
+      if (c0 + CH <= cols) {
+#pragma unroll
+        for (int j = 0; j < CH; ++j) store_y<YT>(y, base + j * ldy, __uint_as_float(r[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < CH; ++j)
+          if (c0 + j < cols) store_y<YT>(y, base + j * ldy, __uint_as_float(r[j]));
+      }
+    }
+  }
+}
+
+
 
 // ---- host side --------------------------------------------------------------
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
