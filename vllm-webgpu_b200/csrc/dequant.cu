@@ -323,6 +323,8 @@ cudaError_t dequant_device_error(int* v, int clear, cudaStream_t st) { return tu
 template <int XT>
 __global__ void __launch_bounds__(256) cast_x_f16_scalar_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                                          int64_t ldx, __half* __restrict__ out) {
+  pdl_wait();  // x may come from the previous kernel, out may still be read by it
+  pdl_trigger();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const int64_t total = m * k;
   if (i >= total) return;
@@ -348,6 +350,8 @@ __global__ void __launch_bounds__(256) cast_x_f16_scalar_kernel(const void* __re
 template <int XT>
 __global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                                          int64_t ldx, __half* __restrict__ out) {
+  pdl_wait();  // x may come from the previous kernel, out may still be read by it
+  pdl_trigger();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const int64_t total = m * k;
   if (i >= total) return;
@@ -388,16 +392,16 @@ cudaError_t launch_cast_x_f16(const void* x, int x_dtype, int64_t m, int64_t k, 
   __half* o = static_cast<__half*>(out);
   const int es = x_dtype == GGUFMM_F32 ? 4 : 2;
   const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * es) % 16 == 0;
-  if (vec) {
-    if (x_dtype == GGUFMM_F32) cast_x_f16_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-    else if (x_dtype == GGUFMM_F16) cast_x_f16_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-    else cast_x_f16_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-  } else {
-    if (x_dtype == GGUFMM_F32) cast_x_f16_scalar_kernel<GGUFMM_F32><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-    else if (x_dtype == GGUFMM_F16) cast_x_f16_scalar_kernel<GGUFMM_F16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-    else cast_x_f16_scalar_kernel<GGUFMM_BF16><<<blocks, 256, 0, st>>>(x, m, k, ldx, o);
-  }
-  return cudaGetLastError();
+  // programmatic dependent launch: the kernel waits for its predecessor before touching
+  // memory, and the GEMM after it may start its weight stream while it runs
+  void (*fn)(const void*, int64_t, int64_t, int64_t, __half*);
+  if (vec)
+    fn = x_dtype == GGUFMM_F32 ? cast_x_f16_kernel<GGUFMM_F32>
+         : x_dtype == GGUFMM_F16 ? cast_x_f16_kernel<GGUFMM_F16> : cast_x_f16_kernel<GGUFMM_BF16>;
+  else
+    fn = x_dtype == GGUFMM_F32 ? cast_x_f16_scalar_kernel<GGUFMM_F32>
+         : x_dtype == GGUFMM_F16 ? cast_x_f16_scalar_kernel<GGUFMM_F16> : cast_x_f16_scalar_kernel<GGUFMM_BF16>;
+  return pdl_launch(fn, dim3(blocks), dim3(256), 0, st, x, m, k, ldx, o);
 }
 
 }  // namespace ggufmm

@@ -1,26 +1,27 @@
 // gemm_fused.cu -- Q4_K GEMM on the sm_100a tensor cores with the dequantization
-// fused into the pipeline: Y[m, n] = sum_k X[m, k] W[n, k] for any M.
+// fused into the pipeline: Y[m, n] = sum_k X[m, k] W[n, k], M <= 128 (batched decode).
 //
 // The two-pass GEMM (dequantize the whole weight to fp16 in scratch, then a
 // tcgen05 GEMM) moves 4.5 bytes per weight through HBM (0.56 read, 2 written,
 // 2 read again). Here each CTA streams the packed GGUF bytes of its 128 weight
-// rows once (0.56 B per weight) and turns them into fp16 MMA operands in shared
-// memory, next to the tensor cores.
+// rows once (0.56 B per weight) and turns them into the fp16 MMA operand in
+// tensor memory, next to the tensor cores.
 //
 // CTA = 14 warps, one 128 (weight rows, MMA M) x BN (tokens, MMA N) tile:
 //   warp 0       TMA producer: per 128-weight k-block, the rows' 16-byte Q4_K
 //                headers (d, dmin, 6-bit scales) and 64 bytes of nibbles (2-D
-//                uint8 tensor maps, no swizzle), and the activation tile (fp16,
-//                128-byte swizzle); one mbarrier transaction count per stage.
+//                uint8 tensor maps, 64-byte swizzle for the nibbles), and the
+//                activation tile (fp16, 128-byte swizzle); one mbarrier
+//                transaction count per stage.
 //   warps 6..13  dequantizers: thread (row r, half q) decodes the 64 weights of
 //                one nibble chunk to fp32 exactly as gguf-py does
 //                ((d*sc)*q - dmin*m; the product is exact, so one fma), rounds
-//                once to fp16 and writes them in the 128-byte-swizzled K-major
-//                layout tcgen05.mma reads; fence.proxy.async makes the generic
-//                stores visible to the tensor core before the warp arrives.
-//   warp 1       allocates TMEM and issues tcgen05.mma (kind::f16, M=128,
-//                N=BN, K=16) from one elected lane; each stage is committed back
-//                to the producer, the last one to the epilogue.
+//                once to fp16 and stores them with tcgen05.st into TMEM lane r,
+//                where tcgen05.mma reads its A operand.
+//   warp 1       allocates TMEM and issues tcgen05.mma (kind::f16, A in TMEM,
+//                B in shared memory, M=128, N=BN, K=16) from one elected lane;
+//                each stage is committed back to the producer, the last one to
+//                the epilogue.
 //   warps 2..5   epilogue: tcgen05.ld of the fp32 accumulator, transposed
 //                stores of Y.
 // Operand precision is that of the two-pass GEMM: the exact fp32 dequantized
@@ -37,19 +38,7 @@
 namespace ggufmm {
 
 constexpr int kFKB = 128;      // weights per k-block (half a Q4_K superblock)
-constexpr int kFusedThreads(int dq) { return (6 + dq) * 32; }
-
-template <int BN>
-struct FusedSmem {
-  static constexpr uint32_t kA = kTileW * kFKB * 2;  // 2 swizzle atoms of 128 rows x 64 fp16
-  static constexpr uint32_t kB = BN * kFKB * 2;      // 2 atoms of BN rows
-  static constexpr uint32_t kHdr = kTileW * 16;
-  static constexpr uint32_t kQs = kTileW * 64;
-  static constexpr uint32_t kStage = kA + kB + kHdr + kQs;
-  static constexpr int kStages = (224 * 1024) / kStage < 4 ? (224 * 1024) / kStage : 4;
-  static constexpr uint32_t kBarOff = kStages * kStage;
-  static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
-};
+constexpr int kFusedThreads = 14 * 32;
 
 // Two fp32 lanes in one instruction (sm_100 packed f32x2): (m - 2^23) * ds + nd per
 // lane, each lane rounded exactly as the scalar sub and fma would round it.
@@ -65,10 +54,6 @@ __device__ __forceinline__ uint32_t dequant_pair_f16(uint32_t m0, uint32_t m1, u
 }
 __device__ __forceinline__ uint64_t splat2(float f) {
   return (static_cast<uint64_t>(__float_as_uint(f)) << 32) | __float_as_uint(f);
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Exact float of a small non-negative integer (< 2^22).
@@ -89,19 +74,57 @@ struct FusedSegs {
   int tile0[kMaxFusedSegs + 1];
   int row0[kMaxFusedSegs + 1];
   int nseg;
-  const uint8_t* q[kMaxFusedSegs];  // the GGUF blocks themselves (the sc*q kernel's epilogue reads d / dmin)
   int64_t row_bytes;
 };
 
-// DQ dequantizer warps (8: a thread decodes 64 weights of a k-block, 16: 32).
-// blockIdx.z selects k-blocks [z * kb_per, (z + 1) * kb_per); with part != null
-// the CTA writes its fp32 partial sums to part[z][m][row0[s] + row] instead of y.
-template <int BN, int DQ, bool X2>
-__global__ void __launch_bounds__(kFusedThreads(DQ), 1)
-    gemm_fused_q4k_kernel(const __grid_constant__ FusedSegs sg, const __grid_constant__ CUtensorMap tm_x, int ytype,
-                          int m, int k, float* __restrict__ part, int kb_per) {
-  using L = FusedSmem<BN>;
+// ---- the same GEMM with the dequantized operand in tensor memory ----------------
+// tcgen05.mma can read its A operand from TMEM instead of shared memory. Here the
+// dequantizer threads (one weight row = one TMEM lane each) write the fp16 weights
+// of a k-block straight into TMEM with tcgen05.st, and the MMA reads them there:
+// shared memory then carries only the TMA traffic (headers, nibbles, activations)
+// and the nibble reads -- about 1.1 bytes per weight instead of 5.1 with the
+// operand staged through shared memory and read back by the tensor core.
+// TMEM columns: [0, BN) the fp32 accumulator, [128 + 64 s, 128 + 64 (s + 1)) the
+// 128 x 128 fp16 A operand of ring stage s (row = lane, two k per 32-bit column).
+template <int BN, int OCC = 1>
+struct FusedTmemSmem {
+  static constexpr uint32_t kB = BN * kFKB * 2;      // activation tile, 2 SW128 atoms
+  static constexpr uint32_t kHdr = kTileW * 16;
+  static constexpr uint32_t kQs = kTileW * 64;       // 64-byte swizzled nibble rows
+  static constexpr uint32_t kStage = kB + kHdr + kQs;
+  // OCC = 2: two CTAs per SM, each with 256 TMEM columns (accumulator + 3 A stages)
+  static constexpr int kMaxStages = OCC == 2 ? 3 : 6;
+  static constexpr int kStages = (224 * 1024 / OCC) / kStage < kMaxStages ? (224 * 1024 / OCC) / kStage : kMaxStages;
+  static constexpr uint32_t kBarOff = kStages * kStage;
+  static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
+  static constexpr uint32_t kAcol = OCC == 2 ? 64 : 128;  // first A column
+  static constexpr uint32_t kCols = OCC == 2 ? 256 : 512;
+  static_assert(OCC == 1 || BN <= 64, "two CTAs per SM hold at most 64 accumulator columns");
+};
+
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
+template <int BN, int OCC>
+__global__ void __launch_bounds__(kFusedThreads, OCC)
+    gemm_fused_q4k_tmem_kernel(const __grid_constant__ FusedSegs sg, const __grid_constant__ CUtensorMap tm_x,
+                               int ytype, int m, int k, float* __restrict__ part, int kb_per) {
+  using L = FusedTmemSmem<BN, OCC>;
   constexpr int S = L::kStages;
+  constexpr uint32_t kCols = L::kCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -115,15 +138,13 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   while (seg + 1 < sg.nseg && static_cast<int>(blockIdx.y) >= sg.tile0[seg + 1]) ++seg;
   const int m0 = blockIdx.x * BN, n0 = (static_cast<int>(blockIdx.y) - sg.tile0[seg]) * kTileW;
   const int n = sg.n[seg];
-  const CUtensorMap* tm_hdr = &sg.hdr[seg];
-  const CUtensorMap* tm_qs = &sg.qs[seg];
   const int kb0 = blockIdx.z * kb_per;
-  const int nkb = min(k / kFKB - kb0, kb_per);  // k-blocks of this CTA (>= 1)
+  const int nkb = min(k / kFKB - kb0, kb_per);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&afull[s], DQ);
+      mbar_init(&afull[s], 8);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
@@ -131,7 +152,7 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN < 32 ? 32 : BN)
+                 "r"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -140,23 +161,34 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem_d = *tmem_slot;
 
+  pdl_trigger();
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
+      // the weights are read-only: the first stages' blocks stream in before the
+      // previous kernel (which writes x and reads y / the partials) has finished
+      auto load_w = [&](int i) {
         const int s = i % S, kb = kb0 + i;
-        if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
         uint8_t* st = smem + s * L::kStage;
         const int sb = kb >> 1, h = kb & 1;
-        mbar_arrive_expect_tx(&full[s], L::kB + L::kHdr + L::kQs);
-        tma_load_2d(st + L::kA + L::kB, tm_hdr, 144 * sb, n0, &full[s]);
-        tma_load_2d(st + L::kA + L::kB + L::kHdr, tm_qs, 144 * sb + 16 + 64 * h, n0, &full[s]);
-        tma_load_2d(st + L::kA, &tm_x, kb * kFKB, m0, &full[s]);
-        tma_load_2d(st + L::kA + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
+        mbar_arrive_expect_tx(&full[s], L::kStage);
+        tma_load_2d(st + L::kB, &sg.hdr[seg], 144 * sb, n0, &full[s]);
+        tma_load_2d(st + L::kB + L::kHdr, &sg.qs[seg], 144 * sb + 16 + 64 * h, n0, &full[s]);
+      };
+      const int pre = min(S, nkb);
+      for (int i = 0; i < pre; ++i) load_w(i);
+      pdl_wait();
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % S, kb = kb0 + i;
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ((i / S) & 1) ^ 1)) break;
+          load_w(i);
+        }
+        uint8_t* st = smem + s * L::kStage;
+        tma_load_2d(st, &tm_x, kb * kFKB, m0, &full[s]);
+        tma_load_2d(st + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16<BN>();
       for (int i = 0; i < nkb; ++i) {
@@ -164,23 +196,23 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
         const uint32_t par = (i / S) & 1;
         if (!mbar_wait(&full[s], par) || !mbar_wait(&afull[s], par)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
-        const uint32_t b_addr = a_addr + L::kA;
+        const uint32_t b_addr = smem_u32(smem + s * L::kStage);
+        const uint32_t a_col = tmem_d + L::kAcol + 64u * s;
 #pragma unroll
         for (int atom = 0; atom < 2; ++atom) {
-          const uint64_t adesc = umma_smem_desc(a_addr + atom * (kTileW * 128));
           const uint64_t bdesc = umma_smem_desc(b_addr + atom * (BN * 128));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem_d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i > 0 || atom > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tmem_d, a_col + 32 * atom + 8 * kk, bdesc + 2 * kk, idesc,
+                        (i > 0 || atom > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
     }
   } else if (warp < 6) {
-    // ---------------- epilogue ----------------
     const int quad = warp & 3;
+    pdl_wait();  // y / the partials may still be read by the previous kernel
     const bool ok = mbar_wait(accum, 0);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok) {
@@ -189,10 +221,8 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
       const int64_t ldy = sg.ldy[seg];
       const int64_t ntot = sg.row0[sg.nseg], grow = sg.row0[seg] + nrow;
       const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16);
-      // columns per TMEM wait (16 with 16 dequantizer warps: their register budget)
-      constexpr int kEpiChunk = DQ == 16 ? 16 : 32;
+      constexpr int kEpiChunk = 32;
       if (part) {
-        // a warp's 32 rows are one 128-byte store
         float* pz = part + static_cast<int64_t>(blockIdx.z) * m * ntot + grow;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += kEpiChunk) {
@@ -217,27 +247,24 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
       }
     }
   } else {
-    // ---------------- dequantizers ----------------
-    // thread (row r, 64-weight half q of the k-block, part sub of that half): with
-    // 16 warps each half is split in two, a thread then owning 16 of its 32 nibble
-    // bytes (output chunks kc = 2 sub, 2 sub + 1 and the same + 4)
-    constexpr int QPT = DQ / 8;    // threads per (row, half)
-    constexpr int KCH = 4 / QPT;   // low-nibble output chunks per thread
-    const int dt = (warp - 6) * 32 + lane;
-    const int r = dt & (kTileW - 1), qp = dt >> 7;
-    const int q = qp / QPT, sub = qp % QPT;
+    // dequantizers: warp w owns TMEM lanes 32 (w % 4) .. + 31, so thread (row r =
+    // 32 (w % 4) + lane, 64-weight half q of the k-block) writes its own lane
+    const int r = ((warp & 3) << 5) | lane, q = (warp - 6) >> 2;
+    const uint32_t trow = tmem_d + (static_cast<uint32_t>(warp & 3) << 21) + L::kAcol + 32u * q;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % S, kb = kb0 + i;
       if (!mbar_wait(&full[s], (i / S) & 1)) break;
+      // the MMAs that last read this stage's columns completed before the producer
+      // refilled the stage (empty[s] -> full[s])
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       uint8_t* st = smem + s * L::kStage;
-      const uint4 hd = *reinterpret_cast<const uint4*>(st + L::kA + L::kB + r * 16);
-      const uint8_t* qsrc = st + L::kA + L::kB + L::kHdr + r * 64 + q * 32 + sub * (32 / QPT);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(qsrc);
-      const uint4 q1 = QPT == 1 ? *reinterpret_cast<const uint4*>(qsrc + 16) : q0;
-      // nibble chunk c of the superblock: low nibbles = sub-block 2c, high = 2c+1
+      const uint4 hd = *reinterpret_cast<const uint4*>(st + L::kB + r * 16);
+      const uint8_t* qrow = st + L::kB + L::kHdr + r * 64;
+      const int swz = (r >> 1) & 3;  // 64-byte swizzle of the nibble rows
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qrow + (((2 * q) ^ swz) << 4));
+      const uint4 q1 = *reinterpret_cast<const uint4*>(qrow + (((2 * q + 1) ^ swz) << 4));
       const int c = 2 * (kb & 1) + q;
       const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
-      // 6-bit scales/mins (gguf quants.py:479-501), branch-free over c
       const uint32_t hi_sel = 0u - static_cast<uint32_t>(c >> 1);
       const uint32_t scw = ((hd.y & 0x3F3F3F3Fu) & ~hi_sel) | (((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) & hi_sel);
       const uint32_t mw = ((hd.z & 0x3F3F3F3Fu) & ~hi_sel) | ((((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u)) & hi_sel);
@@ -247,36 +274,26 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
       const float ndm_lo = -__fmul_rn(dmin, small_uint_to_float((mw >> sh) & 0xFFu));
       const float ndm_hi = -__fmul_rn(dmin, small_uint_to_float((mw >> (sh + 8)) & 0xFFu));
       const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-      uint8_t* arow = st + q * (kTileW * 128) + r * 128;  // atom q, row r
 #pragma unroll
-      for (int kci = 0; kci < 2 * KCH; ++kci) {  // 16-byte output chunk: 8 consecutive k of the atom
-        // k 0..31 = low nibbles of bytes 0..31, k 32..63 = high nibbles
-        const bool hi = kci >= KCH;
-        const int kk = hi ? kci - KCH : kci;
-        const int kc = sub * KCH + kk + (hi ? 4 : 0);
+      for (int kc = 0; kc < 8; ++kc) {  // 8 consecutive k: low nibbles of bytes 8kc.. or high of 8(kc-4)..
+        const bool hi = kc >= 4;
+        const int kk = hi ? kc - 4 : kc;
         const uint32_t wa = w[kk * 2], wb = w[kk * 2 + 1];
         const int shn = hi ? 4 : 0;
-        const float ds = hi ? dsc_hi : dsc_lo, nd = hi ? ndm_hi : ndm_lo;
-        uint32_t out[4];
-        // four nibbles per mask; each becomes the float 2^23 + q with one byte permute
+        const uint64_t ds2 = splat2(hi ? dsc_hi : dsc_lo), nd2 = splat2(hi ? ndm_hi : ndm_lo);
         const uint32_t na = (wa >> shn) & 0x0F0F0F0Fu, nb = (wb >> shn) & 0x0F0F0F0Fu;
+        uint32_t out[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t src = e < 2 ? na : nb;
           const uint32_t b0 = (2u * e) & 3u;
-          if (X2) {
-            out[e] = dequant_pair_f16(__byte_perm(src, 0x4B000000u, 0x7540u | b0),
-                                      __byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1)), splat2(ds), splat2(nd));
-            continue;
-          }
-          const float q0 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | b0)) - 8388608.f;
-          const float q1 = __uint_as_float(__byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1))) - 8388608.f;
-          __half2 h2 = __floats2half2_rn(fmaf(ds, q0, nd), fmaf(ds, q1, nd));
-          out[e] = *reinterpret_cast<uint32_t*>(&h2);
+          out[e] = dequant_pair_f16(__byte_perm(src, 0x4B000000u, 0x7540u | b0),
+                                    __byte_perm(src, 0x4B000000u, 0x7540u | (b0 + 1)), ds2, nd2);
         }
-        *reinterpret_cast<uint4*>(arow + ((kc ^ (r & 7)) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+        tmem_st4(trow + 64u * s + 4u * kc, out);
       }
-      fence_proxy_async_smem();  // generic-proxy stores -> visible to tcgen05.mma
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[s]);
     }
@@ -285,14 +302,14 @@ __global__ void __launch_bounds__(kFusedThreads(DQ), 1)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(BN < 32 ? 32 : BN)
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(kCols) : "memory");
   }
 }
 
 // ---- host side --------------------------------------------------------------
 // uint8 2-D map over the GGUF bytes [rows, row_bytes], box = box_bytes x 128 rows.
-static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes) {
+static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box_bytes,
+                       CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
@@ -300,7 +317,7 @@ static bool make_map_q(CUtensorMap* map, const void* base, int64_t rows, int64_t
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes), static_cast<cuuint32_t>(kTileW)};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -316,6 +333,8 @@ struct ReduceSegs {
   int nseg;
 };
 __global__ void fused_splitk_reduce_kernel(const float* __restrict__ part, int ks, int m, ReduceSegs rs, int ytype) {
+  pdl_wait();
+  pdl_trigger();
   const int ntot = rs.row0[rs.nseg];
   const int64_t total = static_cast<int64_t>(m) * ntot;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -344,9 +363,9 @@ static int sm_count() {
 // K slices per tile: one CTA per SM, so a launch of `tiles` tiles split ks ways runs
 // ceil(tiles * ks / sms) waves of 1/ks of the work each, plus a fixed cost per wave
 // (pipeline fill, TMEM allocation, epilogue) taken as 8 k-blocks of work.
-static int pick_fused_ksplit(int64_t tiles, int nkb, int64_t m, int64_t n, size_t part_bytes) {
+static int pick_fused_ksplit(int64_t tiles, int nkb, int64_t m, int64_t n, size_t part_bytes, int occ = 1) {
   const int forced = env_int("GGUFMM_FUSED_KSPLIT", -1);
-  const int sms = sm_count();
+  const int sms = sm_count() * occ;
   int best = 1;
   double best_cost = 1e30;
   for (int ks = 1; ks <= 16; ++ks) {
@@ -369,9 +388,8 @@ static bool fill_segs(FusedSegs& sg, ReduceSegs& rs, int nseg, const void* const
   sg.nseg = rs.nseg = nseg;
   sg.row_bytes = row_bytes;
   for (int i = 0; i < nseg; ++i) {
-    if (!make_map_q(&sg.hdr[i], q[i], n[i], row_bytes, 16) || !make_map_q(&sg.qs[i], q[i], n[i], row_bytes, 64))
+    if (!make_map_q(&sg.hdr[i], q[i], n[i], row_bytes, 16) || !make_map_q(&sg.qs[i], q[i], n[i], row_bytes, 64, CU_TENSOR_MAP_SWIZZLE_64B))
       return false;
-    sg.q[i] = static_cast<const uint8_t*>(q[i]);
     sg.y[i] = rs.y[i] = y[i];
     sg.ldy[i] = rs.ldy[i] = ldy[i];
     sg.n[i] = static_cast<int>(n[i]);
@@ -384,39 +402,40 @@ static bool fill_segs(FusedSegs& sg, ReduceSegs& rs, int nseg, const void* const
 // zs_out != nullptr: every K slice (even a single one) leaves its fp32 partials in
 // part_ws and no reduction is launched; *zs_out receives the slice count, for an
 // epilogue pass (ffn_epilogue_kernel) that sums them.
-template <int BN, int DQ, bool X2>
+template <int BN, int OCC>
 static cudaError_t launch_fused_bn(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
                                    int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
                                    size_t part_bytes, cudaStream_t st, int* zs_out = nullptr) {
-  using L = FusedSmem<BN>;
+  constexpr uint32_t kSmem = FusedTmemSmem<BN, OCC>::kTotal;
   FusedSegs sg;
   ReduceSegs rs;
   if (!fill_segs(sg, rs, nseg, q, n, k, y, ldy)) return cudaErrorInvalidValue;
   CUtensorMap mx;
   if (!make_map_f16(&mx, x16, m, k, BN)) return cudaErrorInvalidValue;
-  auto fn = gemm_fused_q4k_kernel<BN, DQ, X2>;
+  auto fn = gemm_fused_q4k_tmem_kernel<BN, OCC>;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   {
     std::lock_guard<std::mutex> lk(g_fused_attr_mu);
     if (!g_fused_attr_done.count({reinterpret_cast<const void*>(fn), dev})) {
-      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::kTotal));
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmem));
       if (e != cudaSuccess) return e;
       g_fused_attr_done.insert({reinterpret_cast<const void*>(fn), dev});
     }
   }
   const int64_t mt = (m + BN - 1) / BN, nt = sg.tile0[nseg], ntot = sg.row0[nseg];
   const int nkb = static_cast<int>(k / kFKB);
-  const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, ntot, part_bytes) : 1;
+  const int ks = part_ws ? pick_fused_ksplit(mt * nt, nkb, m, ntot, part_bytes, OCC) : 1;
   const int kb_per = (nkb + ks - 1) / ks;
   const int zs = (nkb + kb_per - 1) / kb_per;  // slices actually used (each >= 1 k-block)
   float* part = (zs > 1 || zs_out) ? static_cast<float*>(part_ws) : nullptr;
   if (zs_out && (!part || part_bytes < static_cast<size_t>(zs) * m * ntot * 4)) return cudaErrorInvalidValue;
   dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt), static_cast<unsigned>(zs));
-  fn<<<grid, kFusedThreads(DQ), L::kTotal, st>>>(sg, mx, ytype, static_cast<int>(m), static_cast<int>(k), part,
-                                                  kb_per);
-  e = cudaGetLastError();
+  // programmatic dependent launch: the kernel waits for its predecessor itself
+  // (pdl_wait before x, y and the partials) and streams its first weights before that
+  e = pdl_launch(fn, grid, dim3(kFusedThreads), kSmem, st, sg, mx, ytype, static_cast<int>(m), static_cast<int>(k),
+                 part, kb_per);
   if (zs_out) {
     *zs_out = zs;
     return e;
@@ -424,24 +443,28 @@ static cudaError_t launch_fused_bn(int nseg, const void* const* q, const int64_t
   if (e != cudaSuccess || !part) return e;
   const int64_t total = m * ntot;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
-  fused_splitk_reduce_kernel<<<blocks, 256, 0, st>>>(part, zs, static_cast<int>(m), rs, ytype);
-  return cudaGetLastError();
+  return pdl_launch(fused_splitk_reduce_kernel, dim3(blocks), dim3(256), 0, st, static_cast<const float*>(part), zs,
+                    static_cast<int>(m), rs, ytype);
 }
 
-// 8 dequantizer warps with packed f32x2 arithmetic (7-10 % faster than the scalar
-// sub / fma at M = 16..64, same bits). 16 warps of half the weights each measured
-// 5-7 % slower; GGUFMM_FUSED_DQ=16 selects them (scalar), GGUFMM_FUSED_F32X2=0 the
-// scalar 8-warp variant.
+// Two CTAs per SM (M <= 64, 256 TMEM columns each) where the launch has much work --
+// (128-row tile, k-block) units -- so one CTA's pipeline fill and drain overlap the
+// other's steady state and the waves are half as coarse (8B gate/up at M = 16: 45.2 ->
+// 39.2 us, down 24.7 -> 23.1); the small launches (q/k/v, o) measured 1-7 % slower
+// with it. GGUFMM_FUSED_OCC=1 / 2 forces one form.
 template <int BN>
 static cudaError_t launch_fused_dq(int nseg, const void* const* q, const int64_t* n, const void* x16, int64_t m,
                                    int64_t k, void* const* y, int ytype, const int64_t* ldy, void* part_ws,
                                    size_t part_bytes, cudaStream_t st, int* zs_out = nullptr) {
-  static const int dq = env_int("GGUFMM_FUSED_DQ", 8);
-  static const int x2 = env_int("GGUFMM_FUSED_F32X2", 1);
-  if (dq == 16)
-    return launch_fused_bn<BN, 16, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
-  return x2 ? launch_fused_bn<BN, 8, true>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out)
-            : launch_fused_bn<BN, 8, false>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
+  static const int occ_env = env_int("GGUFMM_FUSED_OCC", 0);
+  int64_t units = 0;
+  for (int i = 0; i < nseg; ++i) units += (n[i] + kTileW - 1) / kTileW * (k / kFKB);
+  const int occ = occ_env ? occ_env : (units >= 3000 ? 2 : 1);
+  if constexpr (BN <= 64) {
+    if (occ == 2)
+      return launch_fused_bn<BN, 2>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
+  }
+  return launch_fused_bn<BN, 1>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st, zs_out);
 }
 
 // nseg (1..4) Q4_K weights q[i] (16-byte aligned GGUF blocks [n[i], k/256*144]) times
@@ -485,6 +508,8 @@ cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const
 // One rounding into y's dtype.
 __global__ void ffn_epilogue_kernel(const float* __restrict__ part, int ks, int m, int n, int mode, const void* resid,
                                     int64_t ldr, void* y, int ytype, int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t ntot = mode == 0 ? 2 * static_cast<int64_t>(n) : n;
   const int64_t total = static_cast<int64_t>(m) * n, slice = static_cast<int64_t>(m) * ntot;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -508,9 +533,8 @@ cudaError_t launch_ffn_epilogue(const float* part, int ks, int64_t m, int64_t n,
                                 int64_t ldr, void* y, int ytype, int64_t ldy, cudaStream_t st) {
   const int64_t total = m * n;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8 * 148));
-  ffn_epilogue_kernel<<<blocks, 256, 0, st>>>(part, ks, static_cast<int>(m), static_cast<int>(n), mode, resid, ldr, y,
-                                              ytype, ldy);
-  return cudaGetLastError();
+  return pdl_launch(ffn_epilogue_kernel, dim3(blocks), dim3(256), 0, st, part, ks, static_cast<int>(m),
+                    static_cast<int>(n), mode, resid, ldr, y, ytype, ldy);
 }
 
 cudaError_t launch_gemm_fused_q4k(const void* q, const void* x16, int64_t n, int64_t m, int64_t k, void* y, int ytype,

@@ -133,8 +133,12 @@ class TensorParallelSwiGLU:
             if self._exchange is None:
                 self._exchange = ops.PeerExchange(self.down.n, 8, self.group, act.device)
             return ops.gemv_allreduce(act, self.down, self._exchange, out_dtype=torch.float32)
-        except ValueError:
-            self.fused_allreduce = False  # unsupported shape: NCCL from now on
+        except _lib.GGUFMMValueError as e:
+            # only a shape / alignment the fused kernel does not serve falls back (to
+            # NCCL from now on); a dtype or argument refusal is a caller bug
+            if e.status not in (_lib.ERR_SHAPE, _lib.ERR_ALIGN, _lib.ERR_QTYPE):
+                raise
+            self.fused_allreduce = False
             return None
 
     __call__ = forward
