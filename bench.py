@@ -737,8 +737,11 @@ def run_ours(args, rank: int, world: int) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "breakdown": e2e_parts,
                     "path": ("LlamaB200Model.layer_linears_graph" if world == 1 else "TensorParallelLayerLinears.graph_step")
-                    + " (one CUDA-graph replay per step holding the packed H2D copy from pinned host memory, the "
-                      "projections and the packed D2H copy), and a host wait per step (spin on an event)"},
+                    + " (one CUDA-graph replay per step holding the packed host-to-device copy of the "
+                      "activations from pinned host memory, the projections and the packed device-to-host copy "
+                      "of every output, the copies made by the ggufmm_stage_copy kernel over the bus"
+                    + (", GGUFMM_STAGE_KERNEL=0: copy-engine memcpys" if os.environ.get("GGUFMM_STAGE_KERNEL") == "0" else "")
+                    + "), and a host wait per step (spin on an event)"},
             "gpu_launches": len(GROUPS) * steps * repeats,
             "comm": comm,
             "clocks": clocks,

@@ -111,6 +111,19 @@ int ggufmm_dequantize(const void* q, int qtype, int64_t n_rows, int64_t k,
                       void* out, int out_dtype, void* stream);
 
 /*
+ * Host <-> device staging by a kernel: copies `bytes` from src to dst, either of
+ * which may be page-locked host memory mapped for the device (cudaHostAlloc /
+ * torch pin_memory with unified addressing) or device memory. Replaces the
+ * reference's buffer upload and staging-buffer readback
+ * (vllm_webgpu/webgpu/buffer.py:34, :46-63). Unlike a memcpy, it runs on the SMs
+ * and is launched as a programmatic dependent launch, so inside a captured decode
+ * step it chains with the GEMV launches (which stream their weights while the
+ * activations arrive) instead of handing over to a copy engine. Both pointers
+ * 16-byte aligned; pageable host memory gives GGUFMM_ERR_ARG. Stream-ordered.
+ */
+int ggufmm_stage_copy(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
  * Quantized embedding lookup: out[t, :] = dequantize(row ids[t] of the table) for
  * t < n_ids. Replaces the reference's embedding_lookup dispatch
  * (vllm_webgpu/models/llama.py:170-178, shaders/generic/embedding_lookup.wgsl),

@@ -40,6 +40,7 @@ SIGNATURES = {
     "ggufmm_set_wait_limit": (_I, [ctypes.c_uint32]),
     "ggufmm_dequantize": (_I, [_VP, _I, _I64, _I64, _VP, _I, _VP]),
     "ggufmm_embedding": (_I, [_VP, _I, _I64, _I64, _VP, _I64, _VP, _I, _I64, _VP]),
+    "ggufmm_stage_copy": (_I, [_VP, _VP, _SZ, _VP]),
     "ggufmm_gemv": (_I, [_VP, _I, _I64, _I64, _VP, _I, _I64, _I64, _VP, _I, _I64, _VP]),
     "ggufmm_gemv_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP]),
     "ggufmm_gemm_grouped": (_I, [_I, _VP, _VP, _I, _I64, _VP, _I, _I64, _I64, _VP, _I, _VP, _VP, _SZ, _VP]),

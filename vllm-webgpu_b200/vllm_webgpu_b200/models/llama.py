@@ -168,10 +168,10 @@ class LlamaB200Model(BaseB200Model):
 
         def body():
             for dst, src in stage_in:
-                dst.copy_(src, non_blocking=True)
+                ops.staged_copy(dst, src)
             self.layer_linears(layer, normed, attn_out, ffn_normed, ffn_act, bufs)
             for dst, src in stage_out:
-                dst.copy_(src, non_blocking=True)
+                ops.staged_copy(dst, src)
         if g is None:
             side = torch.cuda.Stream(self.device)
             side.wait_stream(cur)

@@ -98,6 +98,42 @@ def embedding(ids: torch.Tensor, table: GGUFQuantTensor, out: torch.Tensor | Non
     return out
 
 
+def stage_copy(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """dst <- src by a kernel, where one side is page-locked host memory and the other
+    a CUDA tensor (both contiguous, same byte size, 16-byte aligned): the decode step's
+    host <-> device staging on the SMs instead of a copy engine, chained with the
+    projections by programmatic dependent launch. Replaces the reference's buffer
+    upload / staging readback (vllm_webgpu/webgpu/buffer.py:34, :46-63). Ordered on
+    the CUDA tensor's device's current stream."""
+    dev = dst.device if dst.is_cuda else src.device
+    if not dev.type == "cuda":
+        raise ValueError("stage_copy needs a CUDA tensor on one side")
+    host = src if dst.is_cuda else dst
+    if host.device.type == "cpu" and not host.is_pinned():
+        raise ValueError("the host side of stage_copy must be pinned")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("stage_copy needs contiguous tensors")
+    nbytes = dst.numel() * dst.element_size()
+    if nbytes != src.numel() * src.element_size():
+        raise ValueError("stage_copy: byte sizes differ")
+    with torch.cuda.device(dev):
+        st = _lib.lib().ggufmm_stage_copy(dst.data_ptr(), src.data_ptr(), nbytes, _stream(dev))
+    _lib.check(st, "ggufmm_stage_copy")
+    return dst
+
+
+def staged_copy(dst: torch.Tensor, src: torch.Tensor) -> None:
+    """The serving graphs' host <-> device copy: ``stage_copy`` where its conditions
+    hold (GGUFMM_STAGE_KERNEL=0 keeps the copy-engine memcpy), else ``dst.copy_``."""
+    import os
+    if (os.environ.get("GGUFMM_STAGE_KERNEL", "1") != "0" and dst.is_contiguous() and src.is_contiguous()
+            and dst.data_ptr() % 16 == 0 and src.data_ptr() % 16 == 0 and dst.dtype == src.dtype
+            and dst.numel() == src.numel() and (dst.is_cuda != src.is_cuda)):
+        stage_copy(dst, src)
+    else:
+        dst.copy_(src, non_blocking=True)
+
+
 def gemv(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
          out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """Decode GEMV, M <= 8 tokens: out[m, n] = sum_k x[m, k] W[n, k]."""

@@ -259,6 +259,7 @@ class TensorParallelLayerLinears:
         buffers), with optional (destination, source) host <-> device copies of pinned
         buffers captured before and after it: the decode serving loop, one replay per
         step (the NCCL all-reduces are captured with the launches)."""
+        from . import ops
         stage_in, stage_out = list(stage_in), list(stage_out)
         key = (normed.data_ptr(), attn_local.data_ptr(), ffn_normed.data_ptr(), act_local.data_ptr(),
                tuple((k, b.data_ptr()) for k, b in sorted(bufs.items())),
@@ -267,10 +268,10 @@ class TensorParallelLayerLinears:
 
         def body():
             for dst, src in stage_in:
-                dst.copy_(src, non_blocking=True)
+                ops.staged_copy(dst, src)
             self.forward(normed, attn_local, ffn_normed, act_local, bufs)
             for dst, src in stage_out:
-                dst.copy_(src, non_blocking=True)
+                ops.staged_copy(dst, src)
         if g is None:
             cur = torch.cuda.current_stream()
             side = torch.cuda.Stream()
