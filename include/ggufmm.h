@@ -176,7 +176,7 @@ int ggufmm_gemv_grouped(int nseg, const void* const* q, const int64_t* n, int qt
  * separate dispatches (vllm_webgpu/models/llama.py:276-283 and 343-348) when
  * more than 8 tokens are in flight. workspace: at least
  * ggufmm_gemm_workspace_size(qtype, M, max of n_i, K) bytes, 256-byte aligned.
- * Q4_K at M <= 128 runs as ONE fused-dequant launch over all the weights' row
+ * Q4_K at M <= 1024 runs as ONE fused-dequant launch over all the weights' row
  * tiles (the activations cast once); otherwise one ggufmm_gemm per weight.
  */
 int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qtype, int64_t k,
@@ -324,7 +324,7 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k,
  * replacing the reference's gate/up dispatches + gelu_mul shader
  * (vllm_webgpu/models/llama.py:343-352, shaders/generic/gelu_mul.wgsl:14-20) and the
  * o / down dispatch + add shader (llama.py:329-335, 355-363). The GEMM leaves fp32
- * partial sums in the workspace (Q4_K at M <= 128: the fused-dequant kernel, one launch
+ * partial sums in the workspace (Q4_K at M <= 1024: the fused-dequant kernel, one launch
  * for gate and up; otherwise dequantize + tcgen05 GEMM per weight) and one pass sums
  * them in a fixed order, applies the epilogue in fp32 and rounds once into y.
  * workspace: ggufmm_gemm_ffn_workspace_size(qtype, M, N, K, swiglu) bytes, 256-byte

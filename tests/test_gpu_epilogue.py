@@ -54,15 +54,19 @@ def _check_swiglu(y, x, gate, up, rg, ru, qt, n, k):
     assert O.rel_err(g.cpu().numpy(), O.matmul_ref(xn, rg, qt, n, k)) <= TOL
     assert O.rel_err(u.cpu().numpy(), O.matmul_ref(xn, ru, qt, n, k)) <= TOL
     ref = (torch.nn.functional.silu(g.double()) * u.double()).cpu().numpy()
-    assert O.rel_err(y.cpu().numpy(), ref) <= 1e-5
+    # Q4_K runs the fused-dequant GEMM, whose K split can differ between the grouped
+    # launch and the single-weight ones; the tensor core's fp32 accumulation is not
+    # reassociation-exact, so those agree to ~1e-4 of the RMS rather than bit for bit
+    assert O.rel_err(y.cpu().numpy(), ref) <= (1e-3 if qt == O.Q4_K else 1e-5)
 
 
 @pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
-@pytest.mark.parametrize("m", [2, 16, 64, 200])
+@pytest.mark.parametrize("m", [2, 16, 64, 200, 1100])
 def test_swiglu_any_m(cuda, qt, m):
     """M = 2: decode (fused integer GEMV for Q4_K / Q4_0, grouped GEMV + epilogue pass
-    otherwise); M = 16 / 64: the fused-dequant GEMM's partials (Q4_K) or the two-pass
-    GEMM; M = 200: the two-pass GEMM, all with the SwiGLU in the epilogue."""
+    otherwise); M = 16 / 64 / 200: the fused-dequant GEMM's partials (Q4_K; 256-token
+    tiles at 200) or the two-pass GEMM; M = 1100: the two-pass GEMM for every format,
+    all with the SwiGLU in the epilogue."""
     from vllm_webgpu_b200 import ops
     n, k = 1536, 2048
     rg, ru = O.make_weights(n, k, qt, seed=1), O.make_weights(n, k, qt, seed=2)
@@ -73,7 +77,7 @@ def test_swiglu_any_m(cuda, qt, m):
 
 
 @pytest.mark.parametrize("qt", [O.Q4_K, O.Q8_0], ids=["Q4_K", "Q8_0"])
-@pytest.mark.parametrize("m", [3, 32, 160])
+@pytest.mark.parametrize("m", [3, 32, 160, 600])
 def test_residual_any_m_in_place(cuda, qt, m):
     from vllm_webgpu_b200 import ops
     n, k = 1024, 4096

@@ -38,6 +38,14 @@ def test_gemm_small(cuda, qt, m):
     assert _check(qt, m, 1024, 4096) <= TOL
 
 
+@pytest.mark.parametrize("m,n,k", [(129, 1000, 2048), (700, 300, 4096), (1024, 1152, 1024), (1025, 640, 1024)])
+def test_gemm_fused_prefill_tiles(cuda, m, n, k):
+    """Q4_K above one 128-token tile: 256-token tiles of the fused-dequant GEMM (each
+    CTA dequantizes its weight tile for its own token tile) up to M = 1024, ragged token
+    and weight-row tails; M = 1025 takes the two-pass path."""
+    assert _check(O.Q4_K, m, n, k, seed=4) <= TOL
+
+
 @pytest.mark.parametrize("qt", QTYPES, ids=lambda q: QNAMES[q])
 @pytest.mark.parametrize("n,k", [(200, 512), (130, 2048), (4096, 14336)])
 def test_gemm_ragged(cuda, qt, n, k):

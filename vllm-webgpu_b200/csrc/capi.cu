@@ -413,6 +413,18 @@ static bool fused_gemm_enabled() {
   return on;
 }
 
+// Largest M served by the fused-dequant GEMM (GGUFMM_GEMM_FUSED_MAXM). Above it the
+// two-pass path wins: it dequantizes each weight once, the fused GEMM once per
+// 256-token tile (measured, Q4_K 14336 x 4096: M = 512 57.6 vs 94.2 us, M = 2048 equal,
+// M = 8192 0.886 vs 0.812 ms).
+static int64_t fused_gemm_max_m() {
+  static const int64_t v = [] {
+    const char* e = std::getenv("GGUFMM_GEMM_FUSED_MAXM");
+    return e && e[0] ? static_cast<int64_t>(std::atoll(e)) : static_cast<int64_t>(1024);
+  }();
+  return v;
+}
+
 // Two-pass GEMM workspace: [fp16 weight][fp16 activations][fp32 partials of the
 // GEMM's tail split]. The first two are required; the GEMM splits its last wave
 // along K only when the workspace also holds the third.
@@ -444,10 +456,10 @@ int ggufmm_gemm(const void* q, int qtype, int64_t n, int64_t k, const void* x, i
   s = check_device();
   if (s) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (qtype == kQ4_K && m <= 128 && aligned(q, 16) && fused_gemm_enabled()) {
-    // dequantization fused into the tensor-core GEMM (one token tile: every weight is
-    // decoded once): only the fp16 activations need scratch. Above one token tile the
-    // two-pass path dequantizes each weight once instead of once per token tile.
+  if (qtype == kQ4_K && m <= fused_gemm_max_m() && aligned(q, 16) && fused_gemm_enabled()) {
+    // dequantization fused into the tensor-core GEMM: only the fp16 activations need
+    // scratch (and the K split's partials). Above fused_gemm_max_m() the two-pass path,
+    // which dequantizes each weight once instead of once per token tile, is faster.
     cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, workspace, st);
     // the K split's fp32 partials go where the two-pass path keeps the fp16 weight
     const size_t x16_bytes = round256(static_cast<size_t>(m) * k * 2);
@@ -472,7 +484,7 @@ int ggufmm_gemm_grouped(int nseg, const void* const* q, const int64_t* n, int qt
   if (!q || !n || !y || !ldy) return GGUFMM_ERR_ARG;
   if (nseg < 1 || nseg > 4) return GGUFMM_ERR_SHAPE;
   int64_t nmax = 0;
-  bool fused = qtype == kQ4_K && m <= 128 && fused_gemm_enabled();
+  bool fused = qtype == kQ4_K && m <= fused_gemm_max_m() && fused_gemm_enabled();
   for (int i = 0; i < nseg; ++i) {
     const int s = check_matmul_args(q[i], qtype, n[i], k, x, x_dtype, m, ldx, y[i], y_dtype, ldy[i]);
     if (s) return s;
@@ -536,7 +548,7 @@ static int gemm_ffn(int nseg, const void* const* qs, int qtype, int64_t n, int64
   uint8_t* w16 = part + part_bytes;
   cudaError_t e = launch_cast_x_f16(x, x_dtype, m, k, ldx, x16, st);
   int zs = 1;
-  bool fused = qtype == kQ4_K && m <= 128 && fused_gemm_enabled();
+  bool fused = qtype == kQ4_K && m <= fused_gemm_max_m() && fused_gemm_enabled();
   for (int i = 0; i < nseg; ++i) fused = fused && aligned(qs[i], 16);
   if (e == cudaSuccess && fused) {
     const int64_t ns[2] = {n, n};

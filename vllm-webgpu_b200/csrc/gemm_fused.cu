@@ -1,5 +1,5 @@
 // gemm_fused.cu -- Q4_K GEMM on the sm_100a tensor cores with the dequantization
-// fused into the pipeline: Y[m, n] = sum_k X[m, k] W[n, k], M <= 128 (batched decode).
+// fused into the pipeline: Y[m, n] = sum_k X[m, k] W[n, k] (batched decode and short prefill).
 //
 // The two-pass GEMM (dequantize the whole weight to fp16 in scratch, then a
 // tcgen05 GEMM) moves 4.5 bytes per weight through HBM (0.56 read, 2 written,
@@ -97,9 +97,10 @@ struct FusedTmemSmem {
   static constexpr int kStages = (224 * 1024 / OCC) / kStage < kMaxStages ? (224 * 1024 / OCC) / kStage : kMaxStages;
   static constexpr uint32_t kBarOff = kStages * kStage;
   static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
-  static constexpr uint32_t kAcol = OCC == 2 ? 64 : 128;  // first A column
+  static constexpr uint32_t kAcol = OCC == 2 ? 64 : (BN > 128 ? BN : 128);  // first A column
   static constexpr uint32_t kCols = OCC == 2 ? 256 : 512;
   static_assert(OCC == 1 || BN <= 64, "two CTAs per SM hold at most 64 accumulator columns");
+  static_assert(kAcol + 64 * kStages <= kCols, "accumulator and operand stages exceed the TMEM allocation");
 };
 
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
@@ -477,15 +478,19 @@ cudaError_t launch_gemm_fused_q4k_grouped(int nseg, const void* const* q, const 
   if (nseg < 1 || nseg > kMaxFusedSegs) return cudaErrorInvalidValue;
   if (m <= 32) return launch_fused_dq<32>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
   if (m <= 64) return launch_fused_dq<64>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
-  return launch_fused_dq<128>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  if (m <= 128) return launch_fused_dq<128>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
+  // prefill: 256-token tiles; each CTA dequantizes its weight tile again for its token
+  // tile, on the ALU while the tensor core works (a k-block's MMAs take about as long
+  // as its dequantization), so the fp16 weight never goes through HBM
+  return launch_fused_dq<256>(nseg, q, n, x16, m, k, y, ytype, ldy, part_ws, part_bytes, st);
 }
 
 // The fused GEMM leaving fp32 partials [zs][m][sum of n] in part_ws for an epilogue
-// pass (m <= 128); *zs_out = the K slices.
+// pass; *zs_out = the K slices.
 cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const int64_t* n, const void* x16,
                                            int64_t m, int64_t k, void* part_ws, size_t part_bytes, int* zs_out,
                                            cudaStream_t st) {
-  if (nseg < 1 || nseg > kMaxFusedSegs || m > 128) return cudaErrorInvalidValue;
+  if (nseg < 1 || nseg > kMaxFusedSegs) return cudaErrorInvalidValue;
   void* ys[kMaxFusedSegs] = {};
   int64_t lds[kMaxFusedSegs] = {};
   for (int i = 0; i < nseg; ++i) {
@@ -494,7 +499,9 @@ cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const
   }
   if (m <= 32) return launch_fused_dq<32>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
   if (m <= 64) return launch_fused_dq<64>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
-  return launch_fused_dq<128>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
+  if (m <= 128)
+    return launch_fused_dq<128>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
+  return launch_fused_dq<256>(nseg, q, n, x16, m, k, ys, GGUFMM_F32, lds, part_ws, part_bytes, st, zs_out);
 }
 
 // The FFN epilogues, over fp32 partial sums part[ks][m][ntot] (ks K slices summed in

@@ -561,7 +561,7 @@ def gemm(x: torch.Tensor, w: GGUFQuantTensor, out: torch.Tensor | None = None,
 def gemm_grouped(x: torch.Tensor, ws: list[GGUFQuantTensor], outs: list[torch.Tensor] | None = None,
                  out_dtype: torch.dtype | None = None) -> list[torch.Tensor]:
     """GEMM of up to 4 weights sharing the activations (q/k/v or gate/up) at any M;
-    Q4_K at M <= 128 is one fused-dequant launch over all of them."""
+    Q4_K at M <= 1024 is one fused-dequant launch over all of them."""
     if not 1 <= len(ws) <= 4:
         raise ValueError("gemm_grouped takes 1 to 4 weights")
     k, qt = ws[0].k, ws[0].qtype
