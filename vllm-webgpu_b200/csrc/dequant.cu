@@ -323,8 +323,10 @@ cudaError_t dequant_device_error(int* v, int clear, cudaStream_t st) { return tu
 template <int XT>
 __global__ void __launch_bounds__(256) cast_x_f16_scalar_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                                          int64_t ldx, __half* __restrict__ out) {
-  pdl_wait();  // x may come from the previous kernel, out may still be read by it
+  // the next kernel (the GEMM) may start its read-only weight stream now; this one
+  // waits for its predecessor: x may come from it, out may still be read by it
   pdl_trigger();
+  pdl_wait();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const int64_t total = m * k;
   if (i >= total) return;
@@ -350,8 +352,10 @@ __global__ void __launch_bounds__(256) cast_x_f16_scalar_kernel(const void* __re
 template <int XT>
 __global__ void __launch_bounds__(256) cast_x_f16_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                                          int64_t ldx, __half* __restrict__ out) {
-  pdl_wait();  // x may come from the previous kernel, out may still be read by it
+  // the next kernel (the GEMM) may start its read-only weight stream now; this one
+  // waits for its predecessor: x may come from it, out may still be read by it
   pdl_trigger();
+  pdl_wait();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const int64_t total = m * k;
   if (i >= total) return;

@@ -96,7 +96,7 @@ struct FusedTmemSmem {
   static constexpr int kMaxStages = OCC == 2 ? 3 : 6;
   static constexpr int kStages = (224 * 1024 / OCC) / kStage < kMaxStages ? (224 * 1024 / OCC) / kStage : kMaxStages;
   static constexpr uint32_t kBarOff = kStages * kStage;
-  static constexpr uint32_t kTotal = kBarOff + (3 * kStages + 1) * 8 + 16 + 1024;
+  static constexpr uint32_t kTotal = kBarOff + (4 * kStages + 1) * 8 + 16 + 1024;
   static constexpr uint32_t kAcol = OCC == 2 ? 64 : (BN > 128 ? BN : 128);  // first A column
   static constexpr uint32_t kCols = OCC == 2 ? 256 : 512;
   static_assert(OCC == 1 || BN <= 64, "two CTAs per SM hold at most 64 accumulator columns");
@@ -128,10 +128,14 @@ __global__ void __launch_bounds__(kFusedThreads, OCC)
   constexpr uint32_t kCols = L::kCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // full[s]: the stage's weight blocks landed (dequantizers); xfull[s]: its activation
+  // tile landed (MMA) -- separate so the dequantizers can start on the weights, which
+  // are streamed before the previous kernel has finished, without waiting for x
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* afull = full + S;
   uint64_t* empty = afull + S;
-  uint64_t* accum = empty + S;
+  uint64_t* xfull = empty + S;
+  uint64_t* accum = xfull + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,6 +151,7 @@ __global__ void __launch_bounds__(kFusedThreads, OCC)
       mbar_init(&full[s], 1);
       mbar_init(&afull[s], 8);
       mbar_init(&empty[s], 1);
+      mbar_init(&xfull[s], 1);
     }
     mbar_init(accum, 1);
     fence_mbar_init();
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(kFusedThreads, OCC)
         const int s = i % S, kb = kb0 + i;
         uint8_t* st = smem + s * L::kStage;
         const int sb = kb >> 1, h = kb & 1;
-        mbar_arrive_expect_tx(&full[s], L::kStage);
+        mbar_arrive_expect_tx(&full[s], L::kHdr + L::kQs);
         tma_load_2d(st + L::kB, &sg.hdr[seg], 144 * sb, n0, &full[s]);
         tma_load_2d(st + L::kB + L::kHdr, &sg.qs[seg], 144 * sb + 16 + 64 * h, n0, &full[s]);
       };
@@ -185,8 +190,9 @@ __global__ void __launch_bounds__(kFusedThreads, OCC)
           load_w(i);
         }
         uint8_t* st = smem + s * L::kStage;
-        tma_load_2d(st, &tm_x, kb * kFKB, m0, &full[s]);
-        tma_load_2d(st + BN * 128, &tm_x, kb * kFKB + 64, m0, &full[s]);
+        mbar_arrive_expect_tx(&xfull[s], L::kB);
+        tma_load_2d(st, &tm_x, kb * kFKB, m0, &xfull[s]);
+        tma_load_2d(st + BN * 128, &tm_x, kb * kFKB + 64, m0, &xfull[s]);
       }
     }
   } else if (warp == 1) {
@@ -195,7 +201,7 @@ __global__ void __launch_bounds__(kFusedThreads, OCC)
       for (int i = 0; i < nkb; ++i) {
         const int s = i % S;
         const uint32_t par = (i / S) & 1;
-        if (!mbar_wait(&full[s], par) || !mbar_wait(&afull[s], par)) break;
+        if (!mbar_wait(&xfull[s], par) || !mbar_wait(&afull[s], par)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t b_addr = smem_u32(smem + s * L::kStage);
         const uint32_t a_col = tmem_d + L::kAcol + 64u * s;
@@ -334,8 +340,8 @@ struct ReduceSegs {
   int nseg;
 };
 __global__ void fused_splitk_reduce_kernel(const float* __restrict__ part, int ks, int m, ReduceSegs rs, int ytype) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int ntot = rs.row0[rs.nseg];
   const int64_t total = static_cast<int64_t>(m) * ntot;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -515,8 +521,8 @@ cudaError_t launch_gemm_fused_q4k_partials(int nseg, const void* const* q, const
 // One rounding into y's dtype.
 __global__ void ffn_epilogue_kernel(const float* __restrict__ part, int ks, int m, int n, int mode, const void* resid,
                                     int64_t ldr, void* y, int ytype, int64_t ldy) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int64_t ntot = mode == 0 ? 2 * static_cast<int64_t>(n) : n;
   const int64_t total = static_cast<int64_t>(m) * n, slice = static_cast<int64_t>(m) * ntot;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
