@@ -197,7 +197,7 @@ def test_peer_allreduce_two_gpus_eager_and_graph(cuda):
     assert res[0][1] == 0 and res[1][1] == 0
 
 
-def _gather_worker(rank, world, port, q):
+def _gather_worker(rank, world, port, q, dtype_name="float32"):
     import os
 
     import torch.distributed as dist
@@ -207,26 +207,29 @@ def _gather_worker(rank, world, port, q):
     try:
         from vllm_webgpu_b200 import _lib, ops
         from vllm_webgpu_b200.formats import GGUFQuantTensor
-        m, n, k = 300, 2048, 1024
+        m, n, k = (300, 2048, 1024) if dtype_name == "float32" else (1100, 2048, 1024)
         raw = O.make_weights(n, k, O.Q4_K, seed=77)
         w = GGUFQuantTensor(torch.from_numpy(raw).cuda(), O.Q4_K, (n, k))
         r0, r1 = rank * n // world, (rank + 1) * n // world
-        g = ops.PeerGather(m, n, torch.float32, device=torch.device("cuda", rank))
+        g = ops.PeerGather(m, n, getattr(torch, dtype_name), device=torch.device("cuda", rank))
         outs = []
         for it in range(2):
             x = torch.from_numpy(O.make_activations(m, k, seed=5 + it)).to(torch.bfloat16).cuda()
             y = ops.gemm_allgather(x, w.rows(r0, r1), g)
             torch.cuda.synchronize()
-            outs.append(y.cpu().numpy().copy())
+            outs.append(y.float().cpu().numpy().copy())
         q.put((rank, outs, _lib.lib().ggufmm_device_status(1, None)))
     finally:
         dist.destroy_process_group()
 
 
-def test_gemm_allgather_two_gpus(cuda):
+@pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
+def test_gemm_allgather_two_gpus(cuda, dtype_name):
     """The N-split GEMM with the all-gather in its epilogue: each GPU computes half the
     output columns and stores them into both GPUs' outputs; after the device barrier
-    both hold the full product (oracle, 2e-3), bit-identical, twice in a row."""
+    both hold the full product (oracle, 2e-3; bf16 adds half an ulp of each value),
+    bit-identical, twice in a row. bf16 at M = 1100: whole tiles go through the staged
+    16-byte peer stores, the ragged last token tile through per-element stores."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import socket
@@ -237,17 +240,21 @@ def test_gemm_allgather_two_gpus(cuda):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q, dtype_name)) for r in range(2)]
     for p in ps:
         p.start()
     res = dict((r, (o, st)) for r, o, st in (q.get(timeout=240) for _ in range(2)))
     for p in ps:
         p.join(60)
-    m, n, k = 300, 2048, 1024
+    m, n, k = (300, 2048, 1024) if dtype_name == "float32" else (1100, 2048, 1024)
     raw = O.make_weights(n, k, O.Q4_K, seed=77)
     for it in range(2):
         x = torch.from_numpy(O.make_activations(m, k, seed=5 + it)).to(torch.bfloat16).float().numpy()
         ref = O.matmul_ref(x, raw, O.Q4_K, n, k)
         assert np.array_equal(res[0][0][it], res[1][0][it])
-        assert O.rel_err(res[0][0][it], ref) <= TOL
+        if dtype_name == "float32":
+            assert O.rel_err(res[0][0][it], ref) <= TOL
+        else:
+            rms = float(np.sqrt(np.mean(ref * ref)))
+            assert bool(np.all(np.abs(res[0][0][it] - ref) <= TOL * rms + 2.0 ** -8 * np.abs(ref)))
     assert res[0][1] == 0 and res[1][1] == 0

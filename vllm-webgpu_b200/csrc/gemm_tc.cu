@@ -39,6 +39,7 @@ struct PeerOut {
   uint64_t y[8];
   int world;
   int64_t col0;
+  int vec;  // 16-bit outputs, 16-byte aligned rows and bases: staged 16-byte peer stores
 };
 
 __device__ __forceinline__ void store_out(void* y, const PeerOut& po, int ytype, int64_t mm, int64_t ldy, int nrow,
@@ -75,7 +76,9 @@ struct GemmSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStageBytes;
-  static constexpr uint32_t kTotal = kBarOff + (2 * STAGES + 6) * 8 + 16 + 1024;  // + alignment slack
+  // the peer epilogue's transpose tiles: per epilogue warp 16 tokens x 32 rows of 16-bit outputs
+  static constexpr uint32_t kEpiOff = (kBarOff + (2 * STAGES + 6) * 8 + 16 + 15) / 16 * 16;
+  static constexpr uint32_t kTotal = kEpiOff + 4 * 16 * 32 * 2 + 1024;  // + alignment slack
 };
 
 template <int BN, int STAGES>
@@ -341,6 +344,32 @@ __global__ void __launch_bounds__(192, 1)
         drain_tile<BN, GGUFMM_F32>(tbase, y, ldy, m0, m, nrow, n);
       } else if (po.world == 0) {
         drain_tile<BN, GGUFMM_F16>(tbase, y, ldy, m0, m, nrow, n);
+      } else if (po.vec && m0 + BN <= m && n0 + kTileW <= n) {
+        // all-gather in the epilogue, whole tile: 16 tokens at a time through a
+        // transpose tile in shared memory, so each lane stores 16 contiguous bytes (8
+        // outputs of one token) to every GPU -- a warp instruction moves 512 bytes per
+        // GPU instead of 64 with one 2-byte store per lane
+        uint16_t* tt = reinterpret_cast<uint16_t*>(smem + L::kEpiOff) + quad * (16 * 32);
+        const bool bf = ytype == GGUFMM_BF16;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float v = __uint_as_float(r[j]);
+            tt[j * 32 + lane] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+          }
+          __syncwarp();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int ch = lane + 32 * h, jj = ch >> 2, qq = ch & 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(tt + jj * 32 + qq * 8);
+            const int64_t off = static_cast<int64_t>(m0 + c0 + jj) * ldy + po.col0 + n0 + quad * 32 + qq * 8;
+            for (int p = 0; p < po.world; ++p) *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(po.y[p]) + off) = v;
+          }
+          __syncwarp();
+        }
       } else {
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -556,6 +585,9 @@ cudaError_t launch_gemm_f16_peers(const void* w16, const void* x16, int64_t n, i
   for (int i = 0; i < world; ++i) po.y[i] = reinterpret_cast<uint64_t>(ys[i]);
   po.world = world;
   po.col0 = col0;
+  bool vec = ytype != GGUFMM_F32 && ldy % 8 == 0 && col0 % 8 == 0;
+  for (int i = 0; i < world; ++i) vec = vec && (po.y[i] & 15) == 0;
+  po.vec = vec ? 1 : 0;
   return launch_gemm_f16_po(w16, x16, n, m, k, ys[0], ytype, ldy, st, po, part, part_bytes);
 }
 
