@@ -51,6 +51,18 @@ __device__ __forceinline__ void store_out(void* y, const PeerOut& po, int ytype,
   for (int p = 0; p < po.world; ++p) store_y_rt(reinterpret_cast<void*>(po.y[p]), ytype, mm * ldy + po.col0 + nrow, v);
 }
 
+// AND of a predicate over the 4 epilogue warps (named barrier 1, 128 threads).
+__device__ __forceinline__ bool epi_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbarrier.red.and.pred p, 1, 128, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
 // tcgen05.alloc takes a power of two >= 32 columns.
 __host__ __device__ constexpr uint32_t tmem_cols_pow2(uint32_t c) {
   uint32_t p = 32;
@@ -76,7 +88,7 @@ struct GemmSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kBarOff = STAGES * kStageBytes;
-  // the peer epilogue's transpose tiles: per epilogue warp 16 tokens x 32 rows of 16-bit outputs
+  // the peer epilogue's transpose tile: 16 tokens x 128 rows of 16-bit outputs
   static constexpr uint32_t kEpiOff = (kBarOff + (2 * STAGES + 6) * 8 + 16 + 15) / 16 * 16;
   static constexpr uint32_t kTotal = kEpiOff + 4 * 16 * 32 * 2 + 1024;  // + alignment slack
 };
@@ -324,7 +336,9 @@ __global__ void __launch_bounds__(192, 1)
       const int b = i & 1;
       int m0, n0, kb0, kb1;
       const int piece = item(i, m0, n0, kb0, kb1);
-      if (!mbar_wait(&tfull[b], static_cast<uint32_t>((i >> 1) & 1))) break;
+      bool okw = mbar_wait(&tfull[b], static_cast<uint32_t>((i >> 1) & 1));
+      if (po.world > 0) okw = epi_all(okw);  // the peer epilogue syncs the 4 warps: leave together
+      if (!okw) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int nrow = n0 + quad * 32 + lane;
       const uint32_t tbase = tmem_d + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(b) * kAccStride;
@@ -348,9 +362,13 @@ __global__ void __launch_bounds__(192, 1)
         // all-gather in the epilogue, whole tile: 16 tokens at a time through a
         // transpose tile in shared memory, so each lane stores 16 contiguous bytes (8
         // outputs of one token) to every GPU -- a warp instruction moves 512 bytes per
-        // GPU instead of 64 with one 2-byte store per lane
-        uint16_t* tt = reinterpret_cast<uint16_t*>(smem + L::kEpiOff) + quad * (16 * 32);
+        // GPU instead of 64 with one 2-byte store per lane. The condition is the same
+        // for the 4 epilogue warps (one tile), so all of them reach the barriers.
+        // the 4 epilogue warps fill one [16 tokens][128 rows] tile together (named barrier
+        // 1), so each token's 256 bytes go out as 16 contiguous 16-byte stores
+        uint16_t* tt = reinterpret_cast<uint16_t*>(smem + L::kEpiOff);
         const bool bf = ytype == GGUFMM_BF16;
+        const int et = quad * 32 + lane;  // 0..127 over the epilogue warps
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t r[16];
@@ -358,17 +376,17 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float v = __uint_as_float(r[j]);
-            tt[j * 32 + lane] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+            tt[j * kTileW + et] = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
           }
-          __syncwarp();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int ch = lane + 32 * h, jj = ch >> 2, qq = ch & 3;
-            const uint4 v = *reinterpret_cast<const uint4*>(tt + jj * 32 + qq * 8);
-            const int64_t off = static_cast<int64_t>(m0 + c0 + jj) * ldy + po.col0 + n0 + quad * 32 + qq * 8;
+            const int ch = et + 128 * h, jj = ch >> 4, qq = ch & 15;
+            const uint4 v = *reinterpret_cast<const uint4*>(tt + jj * kTileW + qq * 8);
+            const int64_t off = static_cast<int64_t>(m0 + c0 + jj) * ldy + po.col0 + n0 + qq * 8;
             for (int p = 0; p < po.world; ++p) *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(po.y[p]) + off) = v;
           }
-          __syncwarp();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
         }
       } else {
 #pragma unroll 1
